@@ -207,11 +207,11 @@ class TorchKernels:
         return o.reshape(T, H * V).to(out.dtype)
 
     # ------------------------------------------------------------------ routed experts
-    def route_top(self, x, w_router, experts, top, shared):
+    def route_top(self, x, w_router, experts, top, shared, scores="softmax"):
         logits = x.float() @ w_router.t()
         order = torch.sort(logits[:, :experts], dim=-1, descending=True, stable=True).indices[:, :top]
         chosen = torch.gather(logits[:, :experts], 1, order)
-        weight = torch.softmax(chosen, dim=-1)
+        weight = torch.softmax(chosen, dim=-1) if scores == "softmax" else torch.sigmoid(chosen)
         gate = torch.sigmoid(logits[:, experts]) if shared else None
         return order.to(torch.int32), weight, gate
 
@@ -271,8 +271,79 @@ class TorchKernels:
         return (act * u).to(gate_up.dtype)
 
     def activation(self, x, activation, out_dtype):
+        if activation == "gelu_erf":
+            z = x.float()
+            return (0.5 * z * (1 + torch.erf(z * 0.7071067811865476))).to(out_dtype)
         assert activation == "relu2"
         return torch.relu(x.float()).pow(2).to(out_dtype)
+
+    # ------------------------------------------------------------------ Dynamic Tanh around sub-layers, pass mixing
+    @staticmethod
+    def _dyntanh(x, norm):
+        return torch.tanh(norm.alpha * x) * norm.weight + norm.bias
+
+    def add_dyntanh(self, residual, delta, after, mult, norm, out_dtype):
+        if delta is not None:
+            d = delta.to(torch.float32)
+            residual += mult * (self._dyntanh(d, after) if after is not None else d)
+        if norm is None:
+            return None
+        return self._dyntanh(residual, norm).to(out_dtype)
+
+    def concat_cast(self, a, b, out_dtype):
+        return torch.cat([a, b], 1).to(out_dtype)
+
+    # ------------------------------------------------------------------ experts whose weight multiplies their input
+    def input_weighted_experts(self, x, choice, weight, w_gate_up, w_down):
+        T, top = choice.shape
+        inter = w_gate_up.shape[1] // 2
+        out = torch.zeros(T, w_down.shape[1], dtype=torch.float32, device=x.device)
+        for t in range(T):
+            for j in range(top):
+                e = int(choice[t, j])
+                u = (x[t:t + 1].float() * weight[t, j]).to(x.dtype)
+                gu = self.linear(u, w_gate_up[e], out_dtype=torch.float32)
+                g = gu[:, :inter]
+                hidden = (g * torch.sigmoid(g) * gu[:, inter:]).to(x.dtype)
+                out[t] += self.linear(hidden, w_down[e]).float()[0]
+        return out
+
+    # ------------------------------------------------------------------ state-space mixer
+    def state_space(self, proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, eps, heads, vdim, state, groups, norm_groups,
+                    batch, view, write_state=True):
+        T = proj.shape[0]
+        inner, GN = heads * vdim, groups * state
+        C, taps = inner + 2 * GN, conv_w.shape[1]
+        z = proj[:, :inner].float()
+        xin = proj[:, inner:inner + C]
+        dt = torch.nn.functional.softplus(proj[:, inner + C:inner + C + heads].float() + dt_bias, threshold=30.0)
+        decay = torch.exp(-rate * dt)
+        y = torch.empty(T, heads, vdim, dtype=torch.float32, device=proj.device)
+        start, keep = 0, taps - 1
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            kept = view.tail[slot][:keep] if keep > 0 else xin[:0]
+            seq = torch.cat([kept.to(xin.dtype), xin[start:start + n]], 0)
+            acc = conv_b[None, :].repeat(n, 1)
+            for j in range(taps):
+                acc = acc + seq[j:j + n].float() * conv_w[:, j]
+            u = (acc * torch.sigmoid(acc)).to(proj.dtype).float()
+            xs = u[:, :inner].view(n, heads, vdim)
+            B = u[:, inner:inner + GN].view(n, groups, state).repeat_interleave(heads // groups, dim=1)
+            Cm = u[:, inner + GN:].view(n, groups, state).repeat_interleave(heads // groups, dim=1)
+            S = view.state[slot].clone()
+            for i in range(n):
+                t = start + i
+                S = decay[t][:, None, None] * S + (dt[t][:, None] * B[i])[:, :, None] * xs[i][:, None, :]
+                y[t] = torch.einsum("hnp,hn->hp", S, Cm[i]) + skip[:, None] * xs[i]
+            if write_state:
+                view.state[slot] = S
+                if keep > 0:
+                    view.tail[slot][:keep] = seq[-keep:]
+            start += n
+        gated = y.reshape(T, inner) * (z * torch.sigmoid(z))
+        parts = gated.view(T, norm_groups, inner // norm_groups)
+        normed = parts * torch.rsqrt(parts.pow(2).mean(-1, keepdim=True) + eps)
+        return (normed.reshape(T, inner) * norm_w).to(proj.dtype)
 
     # ------------------------------------------------------------------ recurrent mixers
     def lightning_attention(self, proj, batch, view, heads, dim, vdim, decays, write_state=True):
@@ -346,17 +417,22 @@ class TorchKernels:
 
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
-                           write_kv=True):
+                           write_kv=True, whole=False, amplitude=1.0):
         T = qkv.shape[0]
         n_qk = heads + kv_heads
         x = qkv[:, :n_qk * dim].float().clone().view(T, n_qk, dim)
-        if q_norm is not None:
+        if q_norm is not None and whole:
+            q, k = x[:, :heads].reshape(T, -1), x[:, heads:].reshape(T, -1)
+            q = q / torch.sqrt(q.pow(2).mean(-1, keepdim=True) + eps) * q_norm
+            k = k / torch.sqrt(k.pow(2).mean(-1, keepdim=True) + eps) * k_norm
+            x = torch.cat([q.view(T, heads, dim), k.view(T, kv_heads, dim)], 1)
+        elif q_norm is not None:
             x = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
             x = torch.cat([x[:, :heads] * q_norm, x[:, heads:] * k_norm], 1)
         if rotary_dim:
             half = rotary_dim // 2
             angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
-            cos, sin = torch.cos(angles)[:, None, :], torch.sin(angles)[:, None, :]
+            cos, sin = amplitude * torch.cos(angles)[:, None, :], amplitude * torch.sin(angles)[:, None, :]
             a, b = x[..., :half], x[..., half:rotary_dim]
             x = torch.cat([a * cos - b * sin, b * cos + a * sin, x[..., rotary_dim:]], -1)
         qkv[:, :n_qk * dim] = x.reshape(T, n_qk * dim).to(qkv.dtype)

@@ -31,6 +31,8 @@ class Attention(Mixer):
         self.width, self.heads, self.kv_heads, self.head_dim = int(width), int(heads), int(kv_heads), int(head_dim)
         self.prefix, self.position, self.window = prefix, position, window
         self.scale = float(scale) if scale is not None else self.head_dim ** -0.5
+        if position is not None and getattr(position, "amplitude", 1.0) != 1.0:
+            raise ValueError("this mixer's kernels rotate with amplitude 1; the position encoding asks for another one")
 
     def tensor_specs(self):
         q, kv = self.heads * self.head_dim, self.kv_heads * self.head_dim

@@ -164,6 +164,36 @@ class RecurrentStateView:
     slot_list: List[int]
 
 
+@dataclass(frozen=True)
+class MatrixState(CacheRequest):
+    """What a mixer with a matrix-valued recurrence behind a short causal convolution keeps per live request: a
+    float32 state [heads, rows, cols] and the convolution's last `taps - 1` inputs over `channels` channels (compute
+    dtype). Zeroed at admission."""
+
+    heads: int
+    rows: int
+    cols: int
+    channels: int
+    taps: int
+    paged = False
+
+    def storage(self, page_size: int):
+        return {"state": ((self.heads, self.rows, self.cols), torch.float32),
+                "tail": ((max(self.taps - 1, 1), self.channels), None)}
+
+    def view(self, tensors, *, slots, slot_list, **_):
+        return MatrixStateView(state=tensors["state"], tail=tensors["tail"], taps=self.taps, slots=slots, slot_list=slot_list)
+
+
+@dataclass
+class MatrixStateView:
+    state: torch.Tensor         # float32 [max_slots + 1, heads, rows, cols]
+    tail: torch.Tensor          # [max_slots + 1, taps - 1, channels], oldest input first
+    taps: int
+    slots: torch.Tensor         # int32 [segments] on the device
+    slot_list: List[int]
+
+
 @dataclass
 class SlotStateView:
     state: torch.Tensor         # [max_slots + 1, *shape]
@@ -366,9 +396,12 @@ class OutputHead(Part):
 class StreamStep(Part):
     """Something that happens to the residual stream between two entries of the layer order (the start of a
     pass over looped layers, say). forward(x float32 [T, width], embedded float32 [T, width] or None, batch)
-    changes x in place; `needs_embedding` True asks the model to keep the embedding's output for it."""
+    changes x in place, or returns the new stream; `needs_embedding` True asks the model to keep the embedding's
+    output for it. `settles_first` True: the step does more than add to the stream, so a sub-layer output that is
+    still on its way there must have joined it before the step runs."""
 
     needs_embedding = False
+    settles_first = False
 
     def forward(self, x, embedded, batch):
         raise NotImplementedError

@@ -76,3 +76,33 @@ class GatedMLP(FeedForward):
 
 
 register_part("feed_forward", "gated_mlp", GatedMLP)
+
+
+class PlainMLP(FeedForward):
+    """W_down act(W_up h) without a gate; `activation` "gelu_erf" (0.5 z (1 + erf(z / sqrt 2))); `names` = (up, down)
+    after `prefix`. The activation is computed in float32 on the product's output."""
+
+    graph_safe = True
+
+    def __init__(self, width: int, inter: int, prefix: str, activation: str = "gelu_erf", names=("up", "down")):
+        self.width, self.inter, self.prefix, self.activation = int(width), int(inter), prefix, activation
+        self.names = tuple(names)
+        if activation not in ("gelu_erf",):
+            raise ValueError(f"activation {activation!r} is not known; known: ['gelu_erf']")
+
+    def tensor_specs(self):
+        p, (u, d) = self.prefix, self.names
+        return [TensorSpec(p + u, (self.inter, self.width)), TensorSpec(p + d, (self.width, self.inter))]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        p, (u, d) = self.prefix, self.names
+        self.w_up = runtime.matrix(tensors[p + u])
+        self.w_down = runtime.matrix(tensors[p + d])
+
+    def forward(self, x, batch):
+        k = self.runtime.kernels
+        return k.linear(k.activation(k.linear(x, self.w_up), self.activation, x.dtype), self.w_down)
+
+
+register_part("feed_forward", "mlp", PlainMLP)

@@ -203,7 +203,15 @@ class DecoderModel:
             block = self.layers[call.layer]
             view = cache.view(owner, batch)
             for step in self.stream_steps.get(i, ()):
-                step.forward(x, embedded, batch)         # in place; commutes with a delta that is still to be added
+                if getattr(step, "settles_first", False) and delta is not None:
+                    if isinstance(delta, PendingDelta):
+                        delta.settle(x)
+                    elif not (delta is ADDED or isinstance(delta, DeferredNorm)):
+                        k.stream_add_norm(x, [delta])
+                    delta = None
+                moved = step.forward(x, embedded, batch)  # in place (an addition commutes with a delta that is still
+                if moved is not None:                     # to be added), or a new stream
+                    x = moved
             if isinstance(delta, PendingDelta) and not getattr(block, "takes_pending", False):
                 delta.settle(x)                   # a block kind that does not know it: plain addition first
                 delta = None

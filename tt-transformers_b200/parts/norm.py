@@ -92,3 +92,35 @@ class LayerNorm(Norm):
 
 
 register_part("norm", "layernorm", LayerNorm)
+
+
+class DynamicTanh(Norm):
+    """y = tanh(alpha x) * w + b with one learned number alpha: no mean, no variance, every element by itself
+    (Zhu et al., "Transformers without Normalization", 2025). Used before a sub-layer (`forward_add`) and after one by
+    blocks that norm a sub-layer's output before it joins the stream (`after`, `join`). Float32 throughout."""
+
+    def __init__(self, width: int, weight_name: str, bias_name: str, alpha_name: str):
+        self.width, self.weight_name, self.bias_name, self.alpha_name = int(width), weight_name, bias_name, alpha_name
+
+    def tensor_specs(self):
+        return [TensorSpec(self.weight_name, (self.width,)), TensorSpec(self.bias_name, (self.width,)),
+                TensorSpec(self.alpha_name, ())]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.weight = tensors[self.weight_name].to(device=runtime.device, dtype=torch.float32).contiguous()
+        self.bias = tensors[self.bias_name].to(device=runtime.device, dtype=torch.float32).contiguous()
+        self.alpha = float(tensors[self.alpha_name].to(torch.float32))
+
+    def forward_add(self, residual, delta, after: "DynamicTanh" = None, mult: float = 1.0):
+        """residual += mult * (after(delta) if `after` else delta), then this norm of the residual."""
+        if delta is ADDED or isinstance(delta, DeferredNorm):
+            delta = None
+        return self.runtime.kernels.add_dyntanh(residual, delta, after, mult, self, self.runtime.dtype)
+
+    def join(self, residual, delta, mult: float = 1.0):
+        """residual += mult * norm(delta): this norm applied to a sub-layer's output on its way into the stream."""
+        self.runtime.kernels.add_dyntanh(residual, delta, self, mult, None, self.runtime.dtype)
+
+
+register_part("norm", "dyntanh", DynamicTanh)

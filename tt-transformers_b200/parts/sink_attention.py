@@ -1,11 +1,15 @@
 """Grouped-query attention with the options of recent decoders, each a parameter:
 
     q, k, v = W_q h, W_k h, W_v h           (query/key size `dim`, value size `vdim`, no biases)
-    qk_norm:   q and k are RMS-normed per head over `dim` with one weight each, shared by the heads, before rotation
-    position:  the first rotary_dim elements of q and k are rotated by the token's position (pairs i, i + rotary_dim/2)
+    qk_norm:   True or "head": q and k are RMS-normed per head over `dim` with one weight each, shared by the heads;
+               "whole": the RMS norm runs over the whole of q (all heads at once) and over the whole of k, with a
+               weight per element of the projection; before rotation either way
+    position:  the first rotary_dim elements of q and k are rotated by the token's position (pairs i, i + rotary_dim/2),
+               cosines and sines times the encoding's amplitude
     score = (q . k) * scale;  softcap c: score = c tanh(score / c)
     chunk n:   position i sees j <= i with floor(i / n) = floor(j / n) only;  window w: j > i - w
-    sink:      one learned number per head joins the softmax's denominator as exp(sink_h); it has no value
+    sink:      one learned number per head joins the softmax's denominator as exp(sink_h); it has no value;
+    sink_score: the same with one constant for every head and no tensor (0: a one in the denominator)
     out = W_o (heads' weighted sums of v)
 
 Keys (normed, rotated) and values go into cache pages at their positions; pages wholly before a request's
@@ -26,7 +30,8 @@ class SinkAttention(Mixer):
 
     def __init__(self, width: int, heads: int, kv_heads: int, dim: int, vdim: int, scale: float, eps: float, prefix: str,
                  softcap: Optional[float] = None, chunk: Optional[int] = None, window: Optional[int] = None,
-                 sink: bool = False, qk_norm: bool = False, position: Optional[PositionEncoding] = None):
+                 sink: bool = False, qk_norm=False, position: Optional[PositionEncoding] = None,
+                 sink_score: Optional[float] = None):
         if heads % kv_heads:
             raise ValueError(f"heads ({heads}) must be a multiple of kv_heads ({kv_heads})")
         self.width, self.heads, self.kv_heads, self.dim, self.vdim = int(width), int(heads), int(kv_heads), int(dim), int(vdim)
@@ -34,7 +39,13 @@ class SinkAttention(Mixer):
         self.softcap = None if softcap is None else float(softcap)
         self.chunk = None if chunk is None else int(chunk)
         self.window = None if window is None else int(window)
+        if qk_norm not in (False, True, None, "head", "whole"):
+            raise ValueError(f"qk_norm {qk_norm!r} is not known; known: [False, 'head', 'whole']")
         self.sink, self.qk_norm, self.position = bool(sink), bool(qk_norm), position
+        self.whole_norm = qk_norm == "whole"
+        self.sink_score = None if sink_score is None else float(sink_score)
+        if self.sink and self.sink_score is not None:
+            raise ValueError("a learned sink and a constant one exclude each other")
         if self.softcap is not None and not self.softcap > 0:
             raise ValueError("softcap must be positive")
         if self.chunk is not None and self.chunk < 1:
@@ -48,7 +59,9 @@ class SinkAttention(Mixer):
         p, H, G = self.prefix, self.heads, self.kv_heads
         specs = [TensorSpec(p + "q", (H * self.dim, self.width)), TensorSpec(p + "k", (G * self.dim, self.width)),
                  TensorSpec(p + "v", (G * self.vdim, self.width)), TensorSpec(p + "o", (self.width, H * self.vdim))]
-        if self.qk_norm:
+        if self.whole_norm:
+            specs += [TensorSpec(p + "q.norm", (H * self.dim,)), TensorSpec(p + "k.norm", (G * self.dim,))]
+        elif self.qk_norm:
             specs += [TensorSpec(p + "q.norm", (self.dim,)), TensorSpec(p + "k.norm", (self.dim,))]
         if self.sink:
             specs.append(TensorSpec(p + "sink", (H,)))
@@ -63,6 +76,9 @@ class SinkAttention(Mixer):
         self.q_norm = tensors[p + "q.norm"].to(**f32).contiguous() if self.qk_norm else None
         self.k_norm = tensors[p + "k.norm"].to(**f32).contiguous() if self.qk_norm else None
         self.sinks = tensors[p + "sink"].to(**f32).contiguous() if self.sink else None
+        if self.sink_score is not None:
+            self.sinks = torch.full((self.heads,), self.sink_score, **f32)
+        self.amplitude = float(getattr(self.position, "amplitude", 1.0)) if self.position is not None else 1.0
 
     def cache_request(self):
         return PagedKV(self.kv_heads, self.dim, self.window, value_dim=self.vdim, chunk=self.chunk)
@@ -90,8 +106,13 @@ class SinkAttention(Mixer):
         rotation = self.position.rotation() if self.position is not None else None
         inv_freq, rotary_dim = rotation if rotation is not None else (None, 0)
         qkv = projected if projected is not None else k.linear(x, self.w_qkv)
-        k.qk_norm_rope_write(qkv, batch, self.q_norm, self.k_norm, self.eps, inv_freq, rotary_dim, self.heads,
-                             self.kv_heads, self.dim, self.vdim, cache, write_cache)
+        if self.whole_norm or self.amplitude != 1.0:
+            k.qk_norm_rope_write(qkv, batch, self.q_norm, self.k_norm, self.eps, inv_freq, rotary_dim, self.heads,
+                                 self.kv_heads, self.dim, self.vdim, cache, write_cache, whole=self.whole_norm,
+                                 amplitude=self.amplitude)
+        else:
+            k.qk_norm_rope_write(qkv, batch, self.q_norm, self.k_norm, self.eps, inv_freq, rotary_dim, self.heads,
+                                 self.kv_heads, self.dim, self.vdim, cache, write_cache)
         mixed = k.sink_attention(qkv, batch, self.heads, self.kv_heads, self.dim, self.vdim, self.scale, self.softcap,
                                  self.sinks, cache)
         return k.linear(mixed, self.w_o)

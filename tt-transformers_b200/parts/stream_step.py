@@ -1,5 +1,6 @@
 """Steps on the residual stream between two entries of the layer order.
 
+`pass_mix`: the stream becomes W [x ; x0] (below).
 `pass_entry`: what happens at the start of a pass over looped layers. With `add_embedding` the embedding's
 output joins the stream again (every pass but the first), and row `row` of a learned table [rows, width] is
 added to every token's stream: x += (x0 if add_embedding) + table[row]. All in float32, in one kernel.
@@ -31,3 +32,29 @@ class PassEntry(StreamStep):
 
 
 register_part("stream_step", "pass_entry", PassEntry)
+
+
+class PassMix(StreamStep):
+    """The start of a pass as a matrix on the stream and the embedding's output side by side:
+    x <- W [x ; x0], W [width, 2 width] with the stream's columns first. The product's operands take the compute
+    dtype, its sums and the new stream are float32."""
+
+    needs_embedding = True
+    settles_first = True
+
+    def __init__(self, width: int, weight_name: str):
+        self.width, self.weight_name = int(width), weight_name
+
+    def tensor_specs(self):
+        return [TensorSpec(self.weight_name, (self.width, 2 * self.width))]
+
+    def bind(self, tensors, runtime):
+        super().bind(tensors, runtime)
+        self.weight = runtime.matrix(tensors[self.weight_name])
+
+    def forward(self, x, embedded, batch):
+        k = self.runtime.kernels
+        return k.linear(k.concat_cast(x, embedded, self.runtime.dtype), self.weight, out_dtype=torch.float32)
+
+
+register_part("stream_step", "pass_mix", PassMix)

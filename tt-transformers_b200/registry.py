@@ -29,6 +29,7 @@ _ARCHITECTURES: Dict[str, Union[str, Architecture]] = {
     "LlamaForCausalLM": "tt_transformers_b200.models.llama",
     "Bozavik": "tt_transformers_b200.models.bozavik",
     "Pedazen": "tt_transformers_b200.models.pedazen",
+    "Sezanex": "tt_transformers_b200.models.sezanex",
 }
 
 
