@@ -543,6 +543,11 @@ moe_gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_
                         tc_load32(lane_addr + OUT_COLS + c0 + h * 32, up);
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
+                            if (!(limit > 0.f)) {        // no clamps, no unit offset: g sigmoid(alpha g) u
+                                const float g = __uint_as_float(accv[j]);
+                                v[j] = __fdividef(g, 1.f + __expf(-alpha * g)) * __uint_as_float(up[j]);
+                                continue;
+                            }
                             const float g = fminf(__uint_as_float(accv[j]), limit);
                             const float u = fminf(fmaxf(__uint_as_float(up[j]), -limit), limit);
                             v[j] = __fdividef(g, 1.f + __expf(-alpha * g)) * (u + 1.f);

@@ -23,7 +23,7 @@ template <typename T, int TPB>
 __global__ void __launch_bounds__(TPB == 1 ? 1024 : 512)
 route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
                  int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate,
-                 int tokens) {
+                 int tokens, int scores) {
     extern __shared__ __align__(16) float rt_smem[];
     const int wpad = (width + 3) & ~3;
     float* h = rt_smem;                                   // [TPB, wpad]
@@ -97,7 +97,7 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
             if (lane == 0) tk[best] = 1;
             __syncwarp();
             if (j == 0) best_first = best_z;
-            const float p = expf(best_z - best_first);
+            const float p = scores == 1 ? 1.f / (1.f + expf(-best_z)) : expf(best_z - best_first);
             denom += p;
             if (lane == 0) {
                 choice[(size_t)t * top + j] = best;
@@ -105,14 +105,16 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
             }
         }
         __syncwarp();                                      // lane 0's weights are visible to the warp
-        for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
+        if (scores == 0)
+            for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
         if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-zt[experts]));
     }
 }
 
 template <typename T, int TPB>
 static int route_top_launch(const void* x, int ldx, const float* w_router, int tokens, int width, int experts, int top,
-                            int shared, int* choice, float* weight, float* shared_gate, int threads, cudaStream_t stream) {
+                            int shared, int* choice, float* weight, float* shared_gate, int threads, int scores,
+                            cudaStream_t stream) {
     const size_t smem = ((size_t)TPB * (((width + 3) & ~3) + 2 * experts + 1)) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     static TtbOncePerDevice once;
@@ -121,13 +123,16 @@ static int route_top_launch(const void* x, int ldx, const float* w_router, int t
         once.mark();
     }
     ttb_launch(route_top_kernel<T, TPB>, (tokens + TPB - 1) / TPB, threads, smem, stream, (const T*)x, ldx, w_router, width,
-               experts, top, shared, choice, weight, shared_gate, tokens);
+               experts, top, shared, choice, weight, shared_gate, tokens, scores);
     return ttb_launch_status();
 }
 
-TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
-                             int top, int shared, int* choice, float* weight, float* shared_gate, cudaStream_t stream) {
+// scores 0: the chosen experts' weights are the softmax over their logits; 1: each one's own sigmoid(logit), as it is.
+TTB_EXPORT int ttb_route_top_scored(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
+                                    int top, int shared, int* choice, float* weight, float* shared_gate, int scores,
+                                    cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
+    if (scores != 0 && scores != 1) return TTB_ERR_UNSUPPORTED;
     if (!x || !w_router || !choice || !weight || (shared && !shared_gate)) return TTB_ERR_ARGUMENT;
     if (experts < 1 || experts > RT_MAX_EXPERTS || top < 1 || top > experts) return TTB_ERR_UNSUPPORTED;
     if ((width & 3) == 0 && !aligned16(w_router)) return TTB_ERR_ARGUMENT;
@@ -138,12 +143,18 @@ TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_r
     const int most = many ? 16 : 32;
     const int threads = 32 * (rows < 4 ? 4 : (rows > most ? most : rows));
 #define RT_LAUNCH(T)                                                                                                 \
-    (many ? route_top_launch<T, 8>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, stream) \
-          : route_top_launch<T, 1>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, stream))
+    (many ? route_top_launch<T, 8>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream) \
+          : route_top_launch<T, 1>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream))
     if (dtype == TTB_DTYPE_BF16) return RT_LAUNCH(__nv_bfloat16);
     if (dtype == TTB_DTYPE_F32) return RT_LAUNCH(float);
 #undef RT_LAUNCH
     return TTB_ERR_UNSUPPORTED;
+}
+
+TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
+                             int top, int shared, int* choice, float* weight, float* shared_gate, cudaStream_t stream) {
+    return ttb_route_top_scored(x, dtype, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, 0,
+                                stream);
 }
 
 // ---------------------------------------------------------------- grouping
@@ -211,7 +222,9 @@ TTB_EXPORT int ttb_moe_align(const int* choice, int pairs, int experts, int top,
 #define MG_BK 16
 #define MG_THREADS 128
 
+// limit <= 0: no clamps and no unit offset, the plain gated unit g sigmoid(alpha g) u (alpha 1: silu(g) u).
 __device__ __forceinline__ float glu_clamped(float g, float u, float limit, float alpha) {
+    if (!(limit > 0.f)) return g / (1.f + expf(-alpha * g)) * u;
     g = fminf(g, limit);
     u = fminf(fmaxf(u, -limit), limit);
     return g / (1.f + expf(-alpha * g)) * (u + 1.f);
@@ -531,7 +544,7 @@ __global__ void __launch_bounds__(MV_THREADS)
 moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W, long long w_expert_stride,
                       const int* __restrict__ choice, int experts, int top, T* __restrict__ hidden, int N, int K,
                       float limit, float alpha, int pairs, const T* __restrict__ shared_w, T* __restrict__ shared_hidden,
-                      int shared_n, float shared_limit) {
+                      int shared_n, float shared_limit, const float* __restrict__ in_scale) {
     extern __shared__ __align__(16) float mv_x[];          // [K]
     pdl_wait();
     pdl_launch_dependents();
@@ -547,7 +560,12 @@ moe_gemv_first_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ W,
         e = choice[p];
     }
     const T* row = x + (size_t)(is_shared ? p : p / top) * ldx;
-    for (int k = threadIdx.x; k < K; k += MV_THREADS) mv_x[k] = to_float(row[k]);
+    if (in_scale != nullptr && !is_shared) {               // the pair's weight on its input, rounded like a stored row
+        const float s = in_scale[p];
+        for (int k = threadIdx.x; k < K; k += MV_THREADS) mv_x[k] = to_float(from_float<T>(to_float(row[k]) * s));
+    } else {
+        for (int k = threadIdx.x; k < K; k += MV_THREADS) mv_x[k] = to_float(row[k]);
+    }
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int n_begin = (blockIdx.x * (MV_THREADS / 32) + warp) * MV_ROWS_PER_WARP;
@@ -617,7 +635,7 @@ moe_gemv_second_kernel(const T* __restrict__ hidden, const T* __restrict__ W, lo
             rows[i] = W + (size_t)e * w_expert_stride + (size_t)min(n_begin + i, N - 1) * K;
         float d[MV_ROWS_PER_WARP];
         mv_dots<T, VEC, MV_ROWS_PER_WARP>(rows, mv_h + (size_t)j * K, K, lane, d);
-        const float wj = weight[(size_t)t * top + j];
+        const float wj = weight != nullptr ? weight[(size_t)t * top + j] : 1.f;
 #pragma unroll
         for (int i = 0; i < MV_ROWS_PER_WARP; ++i) acc[i] = fmaf(wj, d[i], acc[i]);
     }
@@ -651,13 +669,13 @@ static int moe_gemv_launch(const void* x, int ldx, const void* w_gate_up, const 
                            const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
                            int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
                            const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
-                           float shared_limit, bool glu, cudaStream_t stream);
+                           float shared_limit, bool glu, cudaStream_t stream, const float* in_scale);
 
 TTB_EXPORT int ttb_moe_gemv_plain(const void* x, int ldx, const void* w_up, const void* w_down, const int* choice,
                                   const float* weight, void* hidden, float* out, int dtype, int tokens, int experts, int top,
                                   int inter, int width, cudaStream_t stream) {
     return moe_gemv_launch(x, ldx, w_up, w_down, choice, weight, hidden, nullptr, nullptr, out, dtype, tokens, experts, top, inter,
-                           width, 0.f, 0.f, nullptr, nullptr, nullptr, 0, 0.f, false, stream);
+                           width, 0.f, 0.f, nullptr, nullptr, nullptr, 0, 0.f, false, stream, nullptr);
 }
 
 TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
@@ -667,16 +685,26 @@ TTB_EXPORT int ttb_moe_gemv(const void* x, int ldx, const void* w_gate_up, const
                             float shared_limit, cudaStream_t stream) {
     return moe_gemv_launch(x, ldx, w_gate_up, w_down, choice, weight, hidden, shared_out, shared_gate, out, dtype, tokens, experts,
                            top, inter, width, limit, alpha, shared_gate_up, shared_down, shared_hidden, shared_inter, shared_limit,
-                           true, stream);
+                           true, stream, nullptr);
+}
+
+// Gated experts whose weight multiplies their INPUT: hidden = act(W_gate,e (s x), W_up,e (s x)) with s = in_scale[pair]
+// (s x rounded to the compute type), out[t] = sum_j W_down,e_j hidden[t * top + j]. limit <= 0: silu(g) u for alpha 1.
+TTB_EXPORT int ttb_moe_gemv_scaled(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
+                                   const float* in_scale, void* hidden, float* out, int dtype, int tokens, int experts, int top,
+                                   int inter, int width, float limit, float alpha, cudaStream_t stream) {
+    if (!in_scale) return TTB_ERR_ARGUMENT;
+    return moe_gemv_launch(x, ldx, w_gate_up, w_down, choice, nullptr, hidden, nullptr, nullptr, out, dtype, tokens, experts,
+                           top, inter, width, limit, alpha, nullptr, nullptr, nullptr, 0, 0.f, true, stream, in_scale);
 }
 
 static int moe_gemv_launch(const void* x, int ldx, const void* w_gate_up, const void* w_down, const int* choice,
                            const float* weight, void* hidden, const void* shared_out, const float* shared_gate, float* out,
                            int dtype, int tokens, int experts, int top, int inter, int width, float limit, float alpha,
                            const void* shared_gate_up, const void* shared_down, void* shared_hidden, int shared_inter,
-                           float shared_limit, bool glu, cudaStream_t stream) {
+                           float shared_limit, bool glu, cudaStream_t stream, const float* in_scale) {
     if (tokens == 0) return TTB_OK;
-    if (!x || !w_gate_up || !w_down || !choice || !weight || !hidden || !out) return TTB_ERR_ARGUMENT;
+    if (!x || !w_gate_up || !w_down || !choice || !(weight || in_scale) || !hidden || !out) return TTB_ERR_ARGUMENT;
     if ((shared_out || shared_gate_up) && !shared_gate) return TTB_ERR_ARGUMENT;
     if (shared_gate_up && (!shared_down || !shared_hidden || shared_inter < 1 || shared_out)) return TTB_ERR_ARGUMENT;
     const int pairs = tokens * top;
@@ -693,11 +721,11 @@ static int moe_gemv_launch(const void* x, int ldx, const void* w_gate_up, const 
         if (glu)                                                                                                     \
             ttb_launch(moe_gemv_first_kernel<T, VEC, true>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
                        choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up, \
-                       (T*)shared_hidden, sk, shared_limit);                                                         \
+                       (T*)shared_hidden, sk, shared_limit, in_scale);                                               \
         else                                                                                                         \
             ttb_launch(moe_gemv_first_kernel<T, VEC, false>, g1, MV_THREADS, smem1, stream, (const T*)x, ldx, (const T*)w_gate_up, s1, \
                        choice, experts, top, (T*)hidden, inter, width, limit, alpha, pairs, (const T*)shared_gate_up, \
-                       (T*)shared_hidden, sk, shared_limit);                                                         \
+                       (T*)shared_hidden, sk, shared_limit, in_scale);                                               \
         ttb_launch(moe_gemv_second_kernel<T, VEC>, g2, MV_THREADS, smem2, stream, (const T*)hidden, (const T*)w_down, s2,  \
                    choice, weight, experts, top, (const T*)shared_out, shared_gate, out, width, inter,               \
                    (const T*)(shared_gate_up ? shared_down : nullptr), (const T*)shared_hidden, sk);                 \
@@ -722,7 +750,8 @@ __global__ void moe_combine_kernel(const float* __restrict__ pair_out, const flo
     const float sg = shared_out != nullptr ? shared_gate[t] : 0.f;
     for (int c = threadIdx.x; c < width; c += blockDim.x) {
         float s = 0.f;
-        for (int j = 0; j < top; ++j) s = fmaf(weight[(size_t)t * top + j], pair_out[((size_t)t * top + j) * width + c], s);
+        for (int j = 0; j < top; ++j)
+            s = fmaf(weight != nullptr ? weight[(size_t)t * top + j] : 1.f, pair_out[((size_t)t * top + j) * width + c], s);
         if (shared_out != nullptr) s = fmaf(sg, to_float(shared_out[(size_t)t * width + c]), s);
         out[(size_t)t * width + c] = s;
     }
@@ -731,7 +760,7 @@ __global__ void moe_combine_kernel(const float* __restrict__ pair_out, const flo
 TTB_EXPORT int ttb_moe_combine(const float* pair_out, const float* weight, int top, const void* shared_out, int shared_dtype,
                                const float* shared_gate, float* out, int tokens, int width, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
-    if (!pair_out || !weight || !out || (shared_out && !shared_gate)) return TTB_ERR_ARGUMENT;
+    if (!pair_out || !out || (shared_out && !shared_gate)) return TTB_ERR_ARGUMENT;       // weight null: every weight is 1
     if (shared_out && shared_dtype == TTB_DTYPE_BF16)
         ttb_launch(moe_combine_kernel<__nv_bfloat16>, tokens, 256, 0, stream, pair_out, weight, top,
                    (const __nv_bfloat16*)shared_out, shared_gate, out, width);
@@ -768,5 +797,34 @@ TTB_EXPORT int ttb_glu_clamped(const void* gate_up, void* out, int dtype, int ro
         ttb_launch(glu_clamped_kernel<float>, blocks, 256, 0, stream, (const float*)gate_up, (float*)out, rows, inter, limit, alpha);
     else
         return TTB_ERR_UNSUPPORTED;
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- rows gathered with a weight on each
+// out[i, :] = scale[pair_of[i]] * x[token_of[i], :], rounded to the rows' type: the inputs of experts whose weight stands
+// before their activation, laid out in the grouped order.
+template <typename T>
+__global__ void gather_rows_scaled_kernel(const T* __restrict__ x, int ldx, const int* __restrict__ token_of,
+                                          const int* __restrict__ pair_of, const float* __restrict__ scale, T* __restrict__ out,
+                                          int width) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int i = blockIdx.x;
+    const T* src = x + (size_t)token_of[i] * ldx;
+    const float s = scale[pair_of[i]];
+    for (int c = threadIdx.x; c < width; c += blockDim.x) out[(size_t)i * width + c] = from_float<T>(to_float(src[c]) * s);
+}
+
+TTB_EXPORT int ttb_gather_rows_scaled(const void* x, int dtype, int ldx, const int* token_of, const int* pair_of,
+                                      const float* scale, void* out, int rows, int width, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!x || !token_of || !pair_of || !scale || !out) return TTB_ERR_ARGUMENT;
+    if (dtype == TTB_DTYPE_BF16)
+        ttb_launch(gather_rows_scaled_kernel<__nv_bfloat16>, rows, 128, 0, stream, (const __nv_bfloat16*)x, ldx, token_of, pair_of,
+                   scale, (__nv_bfloat16*)out, width);
+    else if (dtype == TTB_DTYPE_F32)
+        ttb_launch(gather_rows_scaled_kernel<float>, rows, 128, 0, stream, (const float*)x, ldx, token_of, pair_of, scale,
+                   (float*)out, width);
+    else return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();
 }

@@ -101,7 +101,9 @@ class CudaKernels:
                      "ttb_mean_rmsnorm_pair", "ttb_activation", "ttb_lightning_scan", "ttb_causal_conv", "ttb_gated_recurrence",
                      "ttb_paged_attention_generic_ext", "ttb_qk_norm_rope_write", "ttb_route_grouped", "ttb_moe_gemv_plain",
                      "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports",
-                     "ttb_recurrent_token"):
+                     "ttb_recurrent_token", "ttb_add_dyntanh", "ttb_concat_cast", "ttb_qk_whole_norm_rope_write",
+                     "ttb_route_top_scored", "ttb_moe_gemv_scaled", "ttb_gather_rows_scaled", "ttb_conv_silu",
+                     "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -758,19 +760,24 @@ class CudaKernels:
         return res
 
     # ------------------------------------------------------------------ routed experts
-    def route_top(self, x, w_router, experts, top, shared):
-        """Float32 router: the `top` experts with the largest logits per token and the softmax over their logits;
+    _ROUTER_SCORES = {"softmax": 0, "sigmoid": 1}
+
+    def route_top(self, x, w_router, experts, top, shared, scores="softmax"):
+        """Float32 router: the `top` experts with the largest logits per token and the softmax over their logits
+        (`scores` "sigmoid": each chosen expert's own sigmoid(logit) instead, not renormalised);
         with `shared`, row `experts` of w_router gives sigmoid(w . x) per token. -> (int32 [T, top], float32 [T, top],
         float32 [T] or None)."""
+        if scores not in self._ROUTER_SCORES:
+            raise KernelError(f"route_top: scores {scores!r} is not known; known: {sorted(self._ROUTER_SCORES)}")
         T, width = x.shape
         if w_router.dtype != torch.float32 or w_router.shape != (experts + (1 if shared else 0), width) or x.stride(1) != 1:
             raise KernelError("route_top: the router's matrix must be float32 [experts (+ 1), width]")
         choice = torch.empty(T, top, dtype=torch.int32, device=self.device)
         weight = torch.empty(T, top, dtype=torch.float32, device=self.device)
         gate = torch.empty(T, dtype=torch.float32, device=self.device) if shared else None
-        self._check(self.lib.ttb_route_top(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(w_router), T, width,
-                                           experts, top, 1 if shared else 0, self._p(choice), self._p(weight),
-                                           self._p(gate), self._stream()), "route_top")
+        self._check(self.lib.ttb_route_top_scored(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(w_router), T, width,
+                                                  experts, top, 1 if shared else 0, self._p(choice), self._p(weight),
+                                                  self._p(gate), self._ROUTER_SCORES[scores], self._stream()), "route_top")
         return choice, weight, gate
 
     def glu_clamped(self, gate_up, limit, alpha):
@@ -912,7 +919,7 @@ class CudaKernels:
                     "mean_rmsnorm_pair")
         return out
 
-    _ACTIVATIONS = {"silu": 0, "gelu_tanh": 1, "relu2": 2}
+    _ACTIVATIONS = {"silu": 0, "gelu_tanh": 1, "relu2": 2, "gelu_erf": 3}
 
     def glu_activation(self, gate_up, activation):
         """act(gate) * up over [rows, gate | up] -> [rows, columns / 2]; activation "silu" or "gelu_tanh"."""
@@ -926,10 +933,11 @@ class CudaKernels:
         return out
 
     def activation(self, x, activation, out_dtype):
-        """An activation element by element ("relu2": relu(z)^2), computed in float32 -> out_dtype."""
+        """An activation element by element ("relu2": relu(z)^2; "gelu_erf": 0.5 z (1 + erf(z / sqrt 2))), computed in
+        float32 -> out_dtype."""
         rows, cols = x.shape
-        if x.stride(1) != 1 or activation != "relu2":
-            raise KernelError("activation: contiguous columns; relu2")
+        if x.stride(1) != 1 or activation not in ("relu2", "gelu_erf"):
+            raise KernelError("activation: contiguous columns; relu2 or gelu_erf")
         out = torch.empty(rows, cols, dtype=out_dtype, device=self.device)
         self._check(self.lib.ttb_activation(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(out), _dtype_code(out_dtype),
                                             rows, cols, self._ACTIVATIONS[activation], self._stream()), "activation")
@@ -1029,10 +1037,31 @@ class CudaKernels:
 
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
-                           write_kv=True):
+                           write_kv=True, whole=False, amplitude=1.0):
         """In place on qkv [T, heads * dim | kv_heads * dim | kv_heads * vdim]: RMS norm per head of q and k (weights
-        float32 [dim] or None), rotation of their first rotary_dim elements; keys and values go into their pages."""
+        float32 [dim] or None), rotation of their first rotary_dim elements; keys and values go into their pages.
+        whole: one RMS norm over all of a token's query elements and one over all of its key elements (weights float32
+        [heads * dim] and [kv_heads * dim]); amplitude: what the rotation's cosines and sines are multiplied by."""
         tokens = qkv.shape[0]
+        if whole or amplitude != 1.0:
+            if q_norm is not None and not whole:
+                raise KernelError("qk_norm_rope_write: a rotation amplitude comes with the norm over the whole projection, or none")
+            if q_norm is not None and (q_norm.shape[0] != heads * dim or k_norm.shape[0] != kv_heads * dim):
+                raise KernelError("qk_norm_rope_write: whole-projection norms need a weight per element of q and of k")
+            if qkv.shape[1] != (heads + kv_heads) * dim + kv_heads * vdim or qkv.stride(1) != 1:
+                raise KernelError("qk_norm_rope_write: qkv must be [tokens, heads * dim + kv_heads * (dim + vdim)], contiguous along its columns")
+            write = bool(write_kv and view is not None)
+            if write and (view.keys.dtype != qkv.dtype or not view.keys.is_contiguous() or not view.values.is_contiguous()):
+                raise KernelError("qk_norm_rope_write: cache pages must be contiguous and of the compute dtype")
+            self._check(self.lib.ttb_qk_whole_norm_rope_write(
+                self._p(qkv), _dtype_code(qkv.dtype), qkv.stride(0), self._p(batch.positions), self._p(batch.seg_of_token),
+                self._p(q_norm), self._p(k_norm), ctypes.c_float(eps), self._p(inv_freq), int(rotary_dim),
+                ctypes.c_float(amplitude), tokens, heads, kv_heads, dim, vdim, self._p(view.keys if write else None),
+                self._p(view.values if write else None), self._p(view.block_table if write else None),
+                view.block_table.shape[1] if write else 0, view.page_size if write else 1,
+                view.keys.shape[0] if write else 0, 1 if write else 0, self._p(self.status), self._stream()),
+                "qk_whole_norm_rope_write")
+            return
         if qkv.shape[1] != (heads + kv_heads) * dim + kv_heads * vdim or qkv.stride(1) != 1:
             raise KernelError("qk_norm_rope_write: qkv must be [tokens, heads * dim + kv_heads * (dim + vdim)], contiguous along its columns")
         if (q_norm is None) != (k_norm is None):
@@ -1162,6 +1191,152 @@ class CudaKernels:
                 ctypes.c_float(0.0), self._stream()), "moe_down")
         self._check(self.lib.ttb_moe_combine(self._p(pair_out), self._p(weight), top, None, 0, None, self._p(out), T, width,
                                              self._stream()), "moe_combine")
+        return out
+
+    # ------------------------------------------------------------------ Dynamic Tanh around sub-layers, pass mixing
+    def add_dyntanh(self, residual, delta, after, mult, norm, out_dtype):
+        """residual += mult * (after(delta) if after else delta), in place and in float32; then norm(residual) in
+        out_dtype (None when norm is None). `after` and `norm` are Dynamic Tanh parts (weight, bias, alpha):
+        tanh(alpha x) * weight + bias."""
+        rows, width = residual.shape
+        if residual.dtype != torch.float32 or not residual.is_contiguous():
+            raise KernelError("the residual stream is float32 and contiguous")
+        if delta is not None and (delta.shape != residual.shape or delta.stride(1) != 1):
+            raise KernelError("add_dyntanh: delta must have the residual's shape")
+        out = torch.empty(rows, width, dtype=out_dtype, device=self.device) if norm is not None else None
+        self._check(self.lib.ttb_add_dyntanh(
+            self._p(residual), self._p(delta), _dtype_code(delta.dtype) if delta is not None else 0,
+            delta.stride(0) if delta is not None else 0,
+            self._p(after.weight if after is not None else None), self._p(after.bias if after is not None else None),
+            ctypes.c_float(after.alpha if after is not None else 0.0), ctypes.c_float(mult),
+            self._p(norm.weight if norm is not None else None), self._p(norm.bias if norm is not None else None),
+            ctypes.c_float(norm.alpha if norm is not None else 0.0), self._p(out),
+            _dtype_code(out_dtype) if norm is not None else 0, rows, width, self._stream()), "add_dyntanh")
+        return out
+
+    def concat_cast(self, a, b, out_dtype):
+        """[a | b] row by row for two float32 [rows, width] tensors -> [rows, 2 width] in out_dtype."""
+        rows, width = a.shape
+        if a.dtype != torch.float32 or b.dtype != torch.float32 or a.shape != b.shape or not a.is_contiguous() or not b.is_contiguous():
+            raise KernelError("concat_cast: two contiguous float32 tensors of one shape")
+        out = torch.empty(rows, 2 * width, dtype=out_dtype, device=self.device)
+        self._check(self.lib.ttb_concat_cast(self._p(a), self._p(b), self._p(out), _dtype_code(out_dtype), rows, width,
+                                             self._stream()), "concat_cast")
+        return out
+
+    # ------------------------------------------------------------------ experts whose weight multiplies their input
+    def input_weighted_experts(self, x, choice, weight, w_gate_up, w_down):
+        """x [T, width]; choice, weight [T, top]; w_gate_up [E, 2 inter, width]; w_down [E, width, inter] -> float32
+        [T, width]: sum_j expert_e(weight[t, j] * x[t]), e = choice[t, j], expert(u) = W_down (silu(W_gate u) * (W_up u)),
+        summed in the order of j. The weighted input is rounded to the compute dtype like any stored row."""
+        T, width = x.shape
+        E, two_inter, _ = w_gate_up.shape
+        inter, top = two_inter // 2, choice.shape[1]
+        pairs = T * top
+        if x.dtype != w_gate_up.dtype or x.stride(1) != 1 or not w_gate_up.is_contiguous() or not w_down.is_contiguous():
+            raise KernelError("input_weighted_experts: operands must share a dtype and be contiguous")
+        if weight.dtype != torch.float32 or not weight.is_contiguous() or not choice.is_contiguous():
+            raise KernelError("input_weighted_experts: contiguous choices and float32 weights")
+        out = torch.empty(T, width, dtype=torch.float32, device=self.device)
+        hidden = torch.empty(pairs, inter, dtype=x.dtype, device=self.device)
+        code = _dtype_code(x.dtype)
+        no_limit, alpha = ctypes.c_float(0.0), ctypes.c_float(1.0)       # the plain gated unit silu(g) * u
+        if pairs <= self.MOE_GEMV_PAIRS and width * 4 <= 48 * 1024 and top * inter * 4 <= 48 * 1024:
+            # a handful of pairs (decode): every pair streams its expert's rows; the second kernel sums a token's pairs
+            self._check(self.lib.ttb_moe_gemv_scaled(
+                self._p(x), x.stride(0), self._p(w_gate_up), self._p(w_down), self._p(choice), self._p(weight),
+                self._p(hidden), self._p(out), code, T, E, top, inter, width, no_limit, alpha, self._stream()), "moe_gemv_scaled")
+            self.launches += 1
+            return out
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=self.device)
+        order = torch.empty(pairs, dtype=torch.int32, device=self.device)
+        tokens_of = torch.empty(pairs, dtype=torch.int32, device=self.device)
+        pair_out = torch.empty(pairs, width, dtype=torch.float32, device=self.device)
+        grouped = torch.empty(pairs, width, dtype=x.dtype, device=self.device)
+        grouped_tc = (x.dtype == torch.bfloat16 and self.use_tcgen05 is not False and pairs >= self.MOE_TCGEN05_PAIRS
+                      and width % 8 == 0 and inter % 8 == 0)
+        max_tiles = -(-pairs // 128) + E
+        tile_info = torch.empty(2 * max_tiles + 1, dtype=torch.int32, device=self.device) if grouped_tc else None
+        self._check(self.lib.ttb_moe_align(self._p(choice), pairs, E, top, self._p(offsets), self._p(order),
+                                           self._p(tokens_of), self._p(tile_info[1:] if grouped_tc else None),
+                                           self._p(tile_info), 128 if grouped_tc else 0, self._stream()), "moe_align")
+        # the tokens' rows in the grouped order, each times its pair's weight
+        self._check(self.lib.ttb_gather_rows_scaled(self._p(x), code, x.stride(0), self._p(tokens_of), self._p(order),
+                                                    self._p(weight), self._p(grouped), pairs, width, self._stream()),
+                    "gather_rows_scaled")
+        if grouped_tc:
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(grouped), width, self._p(w_gate_up), width, self._p(hidden), inter, 1, self._p(offsets),
+                self._p(order), self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, inter, width,
+                no_limit, alpha, self._p(self.tc_error), self._stream()), "moe_gate_up_tcgen05")
+            self._check(self.lib.ttb_moe_gemm_tcgen05(
+                self._p(hidden), inter, self._p(w_down), inter, self._p(pair_out), width, 0, self._p(offsets),
+                self._p(order), self._p(tile_info[1:]), self._p(tile_info), pairs, E, max_tiles, width, inter,
+                no_limit, alpha, self._p(self.tc_error), self._stream()), "moe_down_tcgen05")
+        else:
+            straight = self._iota(pairs)          # the gathered rows are in the grouped order already
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(grouped), width, self._p(w_gate_up), ctypes.c_longlong(two_inter * width), width, self._p(hidden), inter,
+                code, 1, self._p(offsets), self._p(straight), pairs, E, 1, inter, width, no_limit, alpha, self._stream()),
+                "moe_gate_up")
+            self._check(self.lib.ttb_moe_group_gemm(
+                self._p(hidden), inter, self._p(w_down), ctypes.c_longlong(width * inter), inter, self._p(pair_out), width,
+                code, 0, self._p(offsets), self._p(order), pairs, E, top, width, inter, no_limit, alpha, self._stream()),
+                "moe_down")
+        self._check(self.lib.ttb_moe_combine(self._p(pair_out), None, top, None, 0, None, self._p(out), T, width,
+                                             self._stream()), "moe_combine")
+        return out
+
+    # ------------------------------------------------------------------ state-space mixer
+    STATE_SPACE_PART = 64                   # tokens of one part of a long segment in the state-space recurrence
+    STATE_SPACE_SCRATCH_BYTES = 256 << 20   # most memory for the parts' states; longer parts beyond it
+
+    def state_space(self, proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, eps, heads, vdim, state, groups, norm_groups,
+                    batch, view, write_state=True):
+        """proj [T, z | x B C | dt] (z, x: heads * vdim; B, C: groups * state; dt: heads) -> [T, heads * vdim]:
+        u = silu(conv(x B C) + b) from the request's kept inputs on; dt = softplus(dt + dt_bias); per head
+        S = exp(-rate dt) S + dt B x^T (float32 [state, vdim] in view.state), y = S^T C + skip x; then y * silu(z),
+        RMS-normed in norm_groups equal parts, times norm_w. Leaves the state and the convolution's last inputs in the
+        request's slot."""
+        T = proj.shape[0]
+        inner, GN = heads * vdim, groups * state
+        C, taps = inner + 2 * GN, conv_w.shape[1]
+        if proj.stride(1) != 1 or proj.shape[1] != 2 * inner + 2 * GN + heads:
+            raise KernelError("state_space: the projection must hold z, x, B, C and dt, contiguous along its columns")
+        if (view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, state, vdim)
+                or not view.state.is_contiguous() or view.tail.dtype != proj.dtype or not view.tail.is_contiguous()
+                or view.tail.shape[2] != C or conv_w.shape[0] != C):
+            raise KernelError("state_space: the state must be float32 [slots, heads, state, vdim], the kept inputs of the compute dtype")
+        if not self.lib.ttb_state_space_supports(vdim, state):
+            raise KernelError(f"state_space: a state of {state} x {vdim} per head is more than the kernel holds")
+        code = _dtype_code(proj.dtype)
+        xin = proj[:, inner:inner + C]
+        u = torch.empty(T, C, dtype=proj.dtype, device=self.device)
+        self._check(self.lib.ttb_conv_silu(self._p(xin), code, proj.stride(0), self._p(conv_w), self._p(conv_b),
+                                           self._p(batch.seg_of_token), self._p(batch.cu_seqlens), self._p(view.slots),
+                                           self._p(view.tail), self._p(u), T, C, taps, self._stream()), "conv_silu")
+        # long segments run as parts side by side (three launches: the parts' end states from zero, their start states,
+        # the walk that writes out)
+        part_len, parts, part_state, part_log = self.STATE_SPACE_PART, 1, None, None
+        if batch.max_seg_len >= 3 * part_len:
+            per_part = batch.num_segments * heads * state * vdim * 4
+            while -(-batch.max_seg_len // part_len) * per_part > self.STATE_SPACE_SCRATCH_BYTES and part_len < batch.max_seg_len:
+                part_len *= 2
+            parts = -(-batch.max_seg_len // part_len)
+        if parts > 1:
+            part_state = torch.empty(batch.num_segments * heads * parts * state * vdim, dtype=torch.float32, device=self.device)
+            part_log = torch.empty(batch.num_segments * heads * parts, dtype=torch.float32, device=self.device)
+            self.launches += 2
+        y = torch.empty(T, inner, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_state_space_scan(
+            self._p(u), self._p(proj), code, proj.stride(0), inner, inner + C, self._p(dt_bias), self._p(rate), self._p(skip),
+            self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(y),
+            batch.num_segments, heads, vdim, state, groups, taps, 1 if write_state else 0, self._p(part_state),
+            self._p(part_log), parts, part_len, self._stream()), "state_space_scan")
+        out = torch.empty(T, inner, dtype=proj.dtype, device=self.device)
+        self._check(self.lib.ttb_gate_group_norm(self._p(y), self._p(proj), code, proj.stride(0), self._p(norm_w),
+                                                 ctypes.c_float(eps), self._p(out), code, T, inner, norm_groups,
+                                                 self._stream()), "gate_group_norm")
         return out
 
     def _iota(self, count):
