@@ -72,8 +72,34 @@ def pedazen_config(width, pairs, lightning_heads, heads, kv_heads, head_dim, chu
     return cfg
 
 
+def sezanex_config(width, blocks, ssm_heads, ssm_vdim, state, ssm_groups, heads, kv_heads, head_dim, window, experts, top, ff,
+                   dense_ff, vocab, loop=None):
+    """`blocks` times three state-space layers followed by one layer of windowed softmax attention; the first layer
+    has a dense feed-forward, the others scored experts."""
+    def mamba2():
+        return {"type": "mamba2", "mixer": {"heads": ssm_heads, "vdim": ssm_vdim, "state": state, "groups": ssm_groups,
+                                            "norm_groups": ssm_groups, "conv": 4}}
+
+    def attention():
+        return {"type": "attention", "mixer": {
+            "heads": heads, "kv_heads": kv_heads, "dim": head_dim, "vdim": head_dim, "mask": {"size": window},
+            "rot": {"base": 10000.0, "dims": head_dim, "scaling": {"factor": 4.0, "original": 4096, "fast": 32.0, "slow": 1.0}},
+            "scale": head_dim ** -0.5}}
+
+    moe = {"kind": "moe", "expert": {"ff": ff}, "router": {"experts": experts, "top": top}}
+    layers = []
+    for i in range(blocks):
+        for j in range(3):
+            layers.append(dict(mamba2(), mlp={"kind": "dense", "ff": dense_ff} if i == 0 and j == 0 else moe))
+        layers.append(dict(attention(), mlp=moe))
+    cfg = {"architecture": "Sezanex", "vocab": vocab, "width": width, "norm": {"eps": 1e-5}, "layers": layers}
+    if loop:
+        cfg["loop"] = {"start": loop[0], "stop": loop[1], "times": loop[2]}
+    return cfg
+
+
 def layer_runs(cfg: dict) -> int:
-    """How many layers a token passes in a Pedazen configuration, looped layers counted every time."""
+    """How many layers a token passes in a configuration with a `loop`, looped layers counted every time."""
     loop = cfg.get("loop")
     return len(cfg["layers"]) + ((loop["stop"] - loop["start"]) * (loop["times"] - 1) if loop else 0)
 
@@ -83,7 +109,14 @@ def closest_llama(cfg: dict) -> dict:
     depth and vocabulary. For Bozavik: the same heads (head size = unrotated + rotated query elements), one KV
     head per four heads, and a feed-forward as wide as the experts a token uses plus the shared one. For Pedazen:
     as many layers as a token passes, the heads, KV heads and head size of its softmax attention, and a
-    feed-forward as wide as the experts a token uses."""
+    feed-forward as wide as the experts a token uses. For Sezanex: the same with its windowed attention's heads."""
+    if cfg.get("architecture") == "Sezanex":
+        a = next(l["mixer"] for l in cfg["layers"] if l["type"] == "attention")
+        f = next(l["mlp"] for l in cfg["layers"] if l["mlp"] and l["mlp"]["kind"] == "moe")
+        return {"architectures": ["LlamaForCausalLM"], "hidden_size": cfg["width"], "num_hidden_layers": layer_runs(cfg),
+                "num_attention_heads": a["heads"], "num_key_value_heads": a["kv_heads"], "head_dim": a["dim"],
+                "intermediate_size": f["router"]["top"] * f["expert"]["ff"], "vocab_size": cfg["vocab"], "rms_norm_eps": 1e-5,
+                "max_position_embeddings": 131072, "rope_theta": 500000.0, "tie_word_embeddings": True}
     if cfg.get("architecture") == "Pedazen":
         left = next(l["mixer"]["left"] for l in cfg["layers"] if l["type"] == "parallel")
         f = next(l["mlp"] for l in cfg["layers"] if l["mlp"] and l["mlp"]["kind"] == "moe")
@@ -112,6 +145,13 @@ RANDOM_MODELS.update({
     "pedazen-tiny": pedazen_config(128, 1, 2, 4, 2, 64, 64, 128, 2, 4, 2, 64, 2, 1, 256, 512, loop=(0, 2, 2)),
     "pedazen-a": pedazen_config(1024, 4, 8, 16, 4, 64, 1024, 1024, 8, 16, 4, 512, 4, 2, 2048, 32768, loop=(2, 4, 2)),
     "pedazen-b": pedazen_config(2048, 4, 16, 16, 4, 128, 2048, 2048, 8, 32, 4, 1024, 8, 4, 4096, 65536, loop=(2, 4, 2)),
+})
+
+
+RANDOM_MODELS.update({
+    "sezanex-tiny": sezanex_config(128, 1, 4, 32, 32, 2, 4, 2, 64, 64, 4, 2, 64, 256, 512, loop=(1, 4, 2)),
+    "sezanex-a": sezanex_config(1024, 2, 32, 64, 128, 2, 16, 4, 64, 1024, 16, 4, 512, 2048, 32768, loop=(2, 4, 2)),
+    "sezanex-b": sezanex_config(2048, 2, 64, 64, 128, 4, 16, 4, 128, 2048, 32, 4, 1024, 4096, 65536, loop=(2, 4, 2)),
 })
 
 

@@ -550,6 +550,8 @@ _TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_laten
           "Pedazen": ["stream_add_norm", "lightning_attention", "gated_rmsnorm", "qk_norm_rope_write", "sink_attention",
                       "causal_conv", "heads_linear", "gated_recurrence", "recurrent_token", "mean_rmsnorm_pair", "route_grouped", "plain_experts",
                       "glu_activation", "linear"],
+          "Sezanex": ["add_dyntanh", "state_space", "qk_norm_rope_write", "sink_attention", "route_top", "input_weighted_experts",
+                      "activation", "concat_cast", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
 
@@ -614,6 +616,35 @@ def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: i
                     used = min(experts, tokens * top)
                     add("plain_experts", 2.0 * tokens * 2 * top * ff * width, 2 * used * ff * 2 * width + tokens * width * (2 + 4))
                     add("route_grouped", 2.0 * tokens * experts * width, tokens * width * 2 + experts * width * 4)
+    elif cfg.get("architecture") == "Sezanex":
+        width = cfg["width"]
+        loop = cfg.get("loop")
+        runs = [1 + ((loop["times"] - 1) if loop and loop["start"] <= i < loop["stop"] else 0) for i in range(len(cfg["layers"]))]
+        for layer, times in zip(cfg["layers"], runs):
+            m, f = layer["mixer"], layer["mlp"]
+            for _ in range(times):
+                # per sub-layer: the stream in and out, the sub-layer's output in, h out
+                add("add_dyntanh", 0, (2 if f else 1) * tokens * width * (4 + 4 + 3 + 2))
+                if layer["type"] == "mamba2":
+                    H, P, N, G = m["heads"], m["vdim"], m["state"], m["groups"]
+                    inner, GN = H * P, G * N
+                    # per token and head: the state's decay and update (3 N P) and its read (2 N P), however it is cut;
+                    # z, x, B, C, dt in, the gated and normed output out, the state in and out
+                    add("state_space", 5.0 * tokens * H * N * P,
+                        tokens * ((2 * inner + 2 * GN + H) * 2 + inner * 2) + 2 * len(contexts) * H * N * P * 4)
+                else:
+                    H, G, D, V = m["heads"], m["kv_heads"], m["dim"], m["vdim"]
+                    n = m["mask"]["size"] if m.get("mask") else 1 << 30
+                    seen = [min(pos + 1, n) for ctx in contexts for pos in range(ctx - new_per_request, ctx)]
+                    keys_read = sum(min(ctx, n + new_per_request - 1) for ctx in contexts)
+                    add("sink_attention", 2.0 * H * sum(seen) * (D + V), 2 * (keys_read * G * (D + V) + tokens * H * (D + V)))
+                    add("qk_norm_rope_write", 0, tokens * ((H + G) * D * 2 * 2 + G * (D + V) * 2 + G * V * 2))
+                if f and f["kind"] == "moe":
+                    top, ff, experts = f["router"]["top"], f["expert"]["ff"], f["router"]["experts"]
+                    used = min(experts, tokens * top)
+                    add("input_weighted_experts", 2.0 * tokens * 3 * top * ff * width,
+                        2 * used * ff * 3 * width + tokens * width * (2 + 4))
+                    add("route_top", 2.0 * tokens * experts * width, tokens * width * 2 + experts * width * 4)
     else:
         width, heads, kv, hd = cfg["hidden_size"], cfg["num_attention_heads"], cfg["num_key_value_heads"], cfg["head_dim"]
         for _ in range(cfg["num_hidden_layers"]):
@@ -644,7 +675,7 @@ def _step_kernel_times(engine, family: str, entries_fn, reps: int = 3) -> Dict[s
 
 def run_design_comparison(name: str = "bozavik-a", *, prefill_tokens: int = PREFILL_TOKENS, batch: int = 8,
                           context: int = 4096, steps: int = 32, warmup: int = 4, device: str = "cuda:0") -> dict:
-    """Prefill and decode throughput of a named model of another design (Bozavik, Pedazen; random weights) and of the
+    """Prefill and decode throughput of a named model of another design (Bozavik, Pedazen, Sezanex; random weights) and of the
     dense decoder closest to it at equal size, and, kernel by kernel, how far the design's own kernels are from their
     rooflines beside the like kernels of the dense model (eager steps, CUDA events around each kernel-table call)."""
     from ..engine.step import StepEntry
