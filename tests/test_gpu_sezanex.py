@@ -125,11 +125,13 @@ def test_one_key_carries_the_weight_inside_its_window_only(kernels, dtype, sizes
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("H,P,N,G,R,taps", [(4, 16, 24, 2, 1, 4), (1, 6, 5, 1, 1, 1), (3, 5, 1, 3, 3, 6), (2, 64, 128, 1, 2, 4),
                                             (4, 32, 64, 2, 4, 3), (6, 7, 3, 2, 2, 2), (2, 128, 16, 2, 1, 4), (8, 64, 64, 1, 8, 4),
-                                            (1, 72, 40, 1, 3, 5), (2, 9, 256, 2, 1, 2)])
-def test_state_space_against_its_twin(kernels, twin, dtype, H, P, N, G, R, taps):
+                                            (1, 72, 40, 1, 3, 5), (2, 9, 256, 2, 1, 2), (2, 128, 128, 2, 2, 4), (1, 64, 512, 1, 1, 4)])
+@pytest.mark.parametrize("decay", [1.0, 40.0])
+def test_state_space_against_its_twin(kernels, twin, dtype, H, P, N, G, R, taps, decay):
     """Portions beside single tokens, continuing from a state and kept inputs that are not zero, on slots in any order,
     segments long enough to run as parts side by side; a second step continues from what the first left; a state that
-    must only be read stays as it was."""
+    must only be read stays as it was. With the larger decay rates a few tokens' decays multiply to less than float32
+    holds, some to zero outright: the state then forgets, and nothing may become infinite."""
     g = torch.Generator().manual_seed(H * P + N)
     segs = [(0, 37), (90, 1), (5, 2), (0, 1), (300, 70), (0, 450), (7, 3)]
     slots = [3, 0, 5, 1, 4, 6, 8]
@@ -137,7 +139,7 @@ def test_state_space_against_its_twin(kernels, twin, dtype, H, P, N, G, R, taps)
     C = inner + 2 * GN
     conv_w, conv_b = (0.5 * torch.randn(C, taps, generator=g)).to(DEV), (0.2 * torch.randn(C, generator=g)).to(DEV)
     dt_bias = (torch.randn(H, generator=g) - 0.5).to(DEV)
-    rate = torch.exp(torch.rand(H, generator=g) * 4 - 3).to(DEV)
+    rate = (decay * torch.exp(torch.rand(H, generator=g) * 4 - 3)).to(DEV)
     skip, norm_w = torch.randn(H, generator=g).to(DEV), (1 + 0.3 * torch.randn(inner, generator=g)).to(DEV)
     state = (torch.randn(10, H, N, P, generator=g) * 0.5).to(DEV)
     tail = torch.randn(10, max(taps - 1, 1), C, generator=g).to(DEV, dtype)
