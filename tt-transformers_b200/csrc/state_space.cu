@@ -279,6 +279,7 @@ ss_scan_kernel(const SsScanArgs a) {
 // A tile whose decays' product is below SS_RELATIVE_FLOOR (1 / A_k would leave the float32 range) takes the direct form
 // S_k = a_k S_(k-1) + dt_k B_k x_k^T instead; every thread of the block takes the same branch.
 #define SS_RELATIVE_FLOOR 1e-20f
+#define SS_PTILE 16                  // tokens of a tile of the packed walk; at most a warp, whose lanes sum the step sizes
 
 template <bool V> struct SsForm { static constexpr bool value = V; };
 
@@ -303,10 +304,10 @@ ss_scan_packed_kernel(const SsScanArgs a) {
     const bool active = tid < threads;
     const int inner = a.heads * P, group = head / (a.heads / a.groups);
     float* xs = ss_smem;                                             // [TILE, P, 2]  every x twice: a pair for two rows
-    float* bs = xs + 2 * SS_TILE * P;                                // [TILE, N]     dt B / A (or dt B, direct form)
-    float* cs = bs + SS_TILE * N;                                    // [TILE, N]
-    float* meta = cs + SS_TILE * N;                                  // [4, TILE]     a_k, A_k, dt_k, the tile's log
-    float* ypart = meta + 4 * SS_TILE;                               // [TILE, NG, P]
+    float* bs = xs + 2 * SS_PTILE * P;                                // [TILE, N]     dt B / A (or dt B, direct form)
+    float* cs = bs + SS_PTILE * N;                                    // [TILE, N]
+    float* meta = cs + SS_PTILE * N;                                  // [4, TILE]     a_k, A_k, dt_k, the tile's log
+    float* ypart = meta + 4 * SS_PTILE;                               // [TILE, NG, P]
     const int slot = a.slots[seg];
     float2 S[R / 2][4];
     const int n0 = ng * R;
@@ -327,23 +328,29 @@ ss_scan_packed_kernel(const SsScanArgs a) {
     }
     const float rate = a.rate[head], bias = a.dt_bias[head], skip = a.skip[head];
     float log_sum = 0.f;
-    for (int t0 = t_begin; t0 < t_end; t0 += SS_TILE) {
-        const int nt = min(SS_TILE, t_end - t0);
+    for (int t0 = t_begin; t0 < t_end; t0 += SS_PTILE) {
+        const int nt = min(SS_PTILE, t_end - t0);
         __syncthreads();                                             // the tile before is walked, summed and stored
-        if (tid < nt) {
-            float sum = 0.f, dt = 0.f;
-            for (int j = 0; j <= tid; ++j) {
-                dt = ss_softplus(ss_load(a.proj, a.dtype, (size_t)(t0 + j) * a.ld + a.dt_off + head) + bias);
-                sum += dt;
+        if (tid < 32) {
+            // a lane per token: its step size, then the running sum of the tile's step sizes by shuffles
+            float dt = 0.f;
+            if (tid < nt) dt = ss_softplus(ss_load(a.proj, a.dtype, (size_t)(t0 + tid) * a.ld + a.dt_off + head) + bias);
+            float sum = dt;
+#pragma unroll
+            for (int off = 1; off < SS_PTILE; off *= 2) {
+                const float below = __shfl_up_sync(0xffffffffu, sum, off);
+                if (tid >= off) sum += below;
             }
-            meta[tid] = expf(-rate * dt);
-            meta[SS_TILE + tid] = expf(-rate * sum);
-            meta[2 * SS_TILE + tid] = dt;
-            if (ENDS_ONLY && tid == nt - 1) meta[3 * SS_TILE] = -rate * sum;
+            if (tid < nt) {
+                meta[tid] = expf(-rate * dt);
+                meta[SS_PTILE + tid] = expf(-rate * sum);
+                meta[2 * SS_PTILE + tid] = dt;
+                if (ENDS_ONLY && tid == nt - 1) meta[3 * SS_PTILE] = -rate * sum;
+            }
         }
         __syncthreads();
-        const bool relative = meta[SS_TILE + nt - 1] >= SS_RELATIVE_FLOOR;
-        if (ENDS_ONLY && tid == 0) log_sum += meta[3 * SS_TILE];
+        const bool relative = meta[SS_PTILE + nt - 1] >= SS_RELATIVE_FLOOR;
+        if (ENDS_ONLY && tid == 0) log_sum += meta[3 * SS_PTILE];
         for (int k = warp; k < nt; k += warps) {
             const size_t row = (size_t)(t0 + k) * a.channels;
             for (int p = lane * 4; p < P; p += 128) {
@@ -351,7 +358,7 @@ ss_scan_packed_kernel(const SsScanArgs a) {
                 *reinterpret_cast<float4*>(xs + 2 * (k * P + p)) = make_float4(v.x, v.x, v.y, v.y);
                 *reinterpret_cast<float4*>(xs + 2 * (k * P + p) + 4) = make_float4(v.z, v.z, v.w, v.w);
             }
-            const float scale = relative ? meta[2 * SS_TILE + k] / meta[SS_TILE + k] : meta[2 * SS_TILE + k];
+            const float scale = relative ? meta[2 * SS_PTILE + k] / meta[SS_PTILE + k] : meta[2 * SS_PTILE + k];
             for (int n = lane * 4; n < N; n += 128) {
                 float4 v = ss_load4(a.u, a.dtype, row + inner + group * N + n);
                 v.x *= scale; v.y *= scale; v.z *= scale; v.w *= scale;
@@ -394,7 +401,7 @@ ss_scan_packed_kernel(const SsScanArgs a) {
                         }
                     }
                     if (!ENDS_ONLY) {
-                        const float post = RELATIVE ? meta[SS_TILE + k] : 1.f;
+                        const float post = RELATIVE ? meta[SS_PTILE + k] : 1.f;
                         *reinterpret_cast<float4*>(ypart + ((size_t)k * NG + ng) * P + col * 4) =
                             make_float4(post * (acc[0].x + acc[0].y), post * (acc[1].x + acc[1].y),
                                         post * (acc[2].x + acc[2].y), post * (acc[3].x + acc[3].y));
@@ -404,7 +411,7 @@ ss_scan_packed_kernel(const SsScanArgs a) {
             if (relative) walk(SsForm<true>());
             else walk(SsForm<false>());
             if (relative) {
-                const float last = meta[SS_TILE + nt - 1];
+                const float last = meta[SS_PTILE + nt - 1];
                 const float2 ll = make_float2(last, last);
 #pragma unroll
                 for (int r = 0; r < R / 2; ++r)
@@ -502,7 +509,9 @@ static void ss_scan_packed_launch(const SsScanArgs& a, int segments, int threads
         cudaFuncSetAttribute(ss_scan_packed_kernel<R, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         once.mark();
     }
-    if (ends_only) ttb_launch(ss_scan_packed_kernel<R, true>, grid, threads, smem, stream, a);
+    // the parts' end states need no outputs: without their buffer more blocks fit an SM
+    const size_t ends_smem = (size_t)SS_PTILE * (2 * a.P + 2 * a.N + 4) * sizeof(float);
+    if (ends_only) ttb_launch(ss_scan_packed_kernel<R, true>, grid, threads, ends_smem, stream, a);
     else ttb_launch(ss_scan_packed_kernel<R, false>, grid, threads, smem, stream, a);
 }
 
@@ -513,7 +522,7 @@ static bool ss_plan(int P, int N, int& pc, int& r, int& ng) {
     for (r = 1; r <= 32; r *= 2) {
         ng = (N + r - 1) / r;
         const int threads = cols * ng;
-        if (threads <= 256 || (r == 32 && pc == 1 && threads <= 1024)) return true;
+        if (threads <= (pc == 4 && r < 16 ? 128 : 256) || (r == 32 && pc == 1 && threads <= 1024)) return true;
     }
     return false;
 }
@@ -591,7 +600,7 @@ TTB_EXPORT int ttb_state_space_scan(const void* u, const void* proj, int dtype, 
         }                                                                                      \
     } while (0)
     // the packed walk: whole groups of four columns and of four rows, float32 stores of the state on 16-byte boundaries
-    const size_t packed_smem = smem + (size_t)SS_TILE * (P + 2) * sizeof(float);
+    const size_t packed_smem = ((size_t)SS_PTILE * (2 * P + 2 * N + 4) + (size_t)SS_PTILE * ng * P) * sizeof(float);
     const bool packed = pc == 4 && r >= 4 && N % r == 0 && N % 4 == 0 && threads <= 256 && packed_smem <= 200 * 1024 &&
                         (dtype == TTB_DTYPE_BF16 ? ((uintptr_t)u % 8 == 0) : ((uintptr_t)u % 16 == 0)) &&
                         (uintptr_t)state % 16 == 0 && (uintptr_t)y % 16 == 0 && (parts == 1 || (uintptr_t)part_state % 16 == 0);
