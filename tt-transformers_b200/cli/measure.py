@@ -48,6 +48,13 @@ def peaks() -> dict:
     return {**FALLBACK_PEAKS, "bf16_tflops_sustained": FALLBACK_PEAKS["bf16_tflops"], "source": "fallback"}
 
 
+def fp32_pipe_tflops(device: int = 0) -> float:
+    """What the float32 multiply-add pipe can do: SMs x 128 lanes x 2 FLOPs x the highest SM clock (nominal, not measured)."""
+    props = torch.cuda.get_device_properties(device)
+    mhz = getattr(props, "clock_rate", 0) / 1e3 or 1965.0
+    return props.multi_processor_count * 128 * 2 * mhz * 1e6 / 1e12
+
+
 class ClockSampler:
     """nvidia-smi in the background for the whole run (reading only); a timed region keeps the samples that
     arrived while it ran, or, if the region was shorter than the sampling period, the sample nearest to it."""
@@ -632,6 +639,8 @@ def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: i
                     # z, x, B, C, dt in, the gated and normed output out, the state in and out
                     add("state_space", 5.0 * tokens * H * N * P,
                         tokens * ((2 * inner + 2 * GN + H) * 2 + inner * 2) + 2 * len(contexts) * H * N * P * 4)
+                    # the walk token by token keeps the state float32 on the float32 pipe: two multiply-adds an element
+                    work["state_space"]["fp32_flops"] = work["state_space"].get("fp32_flops", 0.0) + 4.0 * tokens * H * N * P
                 else:
                     H, G, D, V = m["heads"], m["kv_heads"], m["dim"], m["vdim"]
                     n = m["mask"]["size"] if m.get("mask") else 1 << 30
@@ -750,5 +759,8 @@ def _roofline_rows(times: Dict[str, float], work: Dict[str, dict], pk: dict) -> 
             row["roofline_us"] = round(max(t_flops, t_bytes), 2)
             row["bound"] = "tensor" if t_flops > t_bytes else "hbm"
             row["frac"] = round(max(t_flops, t_bytes) / us, 4)
+            if w.get("fp32_flops"):
+                row["fp32_pipe_us"] = round(w["fp32_flops"] / (fp32_pipe_tflops() * 1e12) * 1e6, 2)
+                row["fp32_pipe_frac"] = round(row["fp32_pipe_us"] / us, 4)
         rows[name] = row
     return rows
