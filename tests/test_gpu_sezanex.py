@@ -168,6 +168,41 @@ def test_state_space_against_its_twin(kernels, twin, dtype, H, P, N, G, R, taps,
         segs = [(p + n, m) for (p, n), m in zip(segs, (1, 3, 1, 200, 2, 1, 64))]
 
 
+@pytest.mark.parametrize("H,P,N,G,taps", [(4, 64, 128, 2, 4), (2, 32, 64, 1, 3), (3, 16, 16, 3, 2), (2, 128, 32, 2, 4)])
+@pytest.mark.parametrize("decay", [1.0, 40.0])
+def test_state_space_on_tensor_cores_keeps_float32_where_the_walk_does(kernels, H, P, N, G, taps, decay):
+    """Long bfloat16 segments run as parts on the tensor cores, where every float32 factor enters as two bfloat16
+    halves; the walk token by token (one part however long the segment) on the same inputs holds the state in plain
+    float32. The states they leave agree far below bfloat16's rounding, also where a head forgets within a few tokens,
+    for ragged last parts and for single tokens beside long segments."""
+    g = torch.Generator().manual_seed(7 * H + P + N)
+    segs, slots = [(0, 450), (3, 200), (17, 64), (9, 1), (0, 129)], [2, 0, 4, 1, 5]
+    inner, GN = H * P, G * N
+    C = inner + 2 * GN
+    conv_w, conv_b = (0.5 * torch.randn(C, taps, generator=g)).to(DEV), (0.2 * torch.randn(C, generator=g)).to(DEV)
+    dt_bias = (torch.randn(H, generator=g) - 0.5).to(DEV)
+    rate = (decay * torch.exp(torch.rand(H, generator=g) * 4 - 3)).to(DEV)
+    skip, norm_w = torch.randn(H, generator=g).to(DEV), (1 + 0.3 * torch.randn(inner, generator=g)).to(DEV)
+    state = (torch.randn(7, H, N, P, generator=g) * 0.5).to(DEV)
+    tail = torch.randn(7, taps - 1, C, generator=g).to(DEV, torch.bfloat16)
+    batch = _batch(segs, slots)
+    proj = torch.randn(batch.num_tokens, 2 * inner + 2 * GN + H, generator=g).to(DEV, torch.bfloat16)
+    out, views = [], []
+    part = kernels.STATE_SPACE_PART
+    try:
+        for part_len in (part, 1 << 20):
+            kernels.STATE_SPACE_PART = part_len
+            view = MatrixState(H, N, P, C, taps).view({"state": state.clone(), "tail": tail.clone()}, slots=batch.seg_slot,
+                                                      slot_list=slots)
+            out.append(kernels.state_space(proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, 1e-5, H, P, N, G, G, batch, view))
+            views.append(view)
+    finally:
+        kernels.STATE_SPACE_PART = part
+    _close(views[0].state, views[1].state, 3e-5)
+    assert torch.equal(views[0].tail, views[1].tail)
+    _close(out[0], out[1], 1e-2)                                          # bfloat16 outputs: a unit in the last place
+
+
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_state_space_keeps_a_far_token(kernels, dtype):
     check_state_space_keeps_a_far_token(kernels, DEV, dtype)

@@ -109,6 +109,64 @@ ss_conv_silu4_kernel(const void* __restrict__ in, int dtype, int ld, const float
     }
 }
 
+// Prompt portions: a thread takes four neighbouring channels over SS_CONV_RUN tokens in a row and keeps the last
+// taps - 1 inputs and its taps' weights in registers, so a token costs one load of its own input. The window is read
+// anew at the run's first token and wherever another segment begins. The same sums in the same order as above.
+#define SS_CONV_RUN 8
+template <int TAPS>
+__global__ void __launch_bounds__(128)
+ss_conv_silu_run_kernel(const void* __restrict__ in, int dtype, int ld, const float* __restrict__ conv_w,
+                        const float* __restrict__ conv_b, const int* __restrict__ seg_of_token, const int* __restrict__ cu_seqlens,
+                        const int* __restrict__ slots, const void* __restrict__ tail, void* __restrict__ out, int tokens,
+                        int channels) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int q = blockIdx.y * blockDim.x + threadIdx.x;
+    if (q >= channels / 4) return;
+    const int c = q * 4;
+    const int t_first = blockIdx.x * SS_CONV_RUN, t_last = min(tokens, t_first + SS_CONV_RUN);
+    float w[4][TAPS];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < TAPS; ++j) w[i][j] = conv_w[(size_t)(c + i) * TAPS + j];
+    const float4 bias = *reinterpret_cast<const float4*>(conv_b + c);
+    float4 win[TAPS];                                            // win[j]: the input TAPS - 1 - j tokens back
+    int seg = -1, seg_begin = 0;
+    size_t kept = 0;
+    for (int t = t_first; t < t_last; ++t) {
+        const int s = seg_of_token[t];
+        const bool fresh = t == t_first || s != seg;
+        if (s != seg) {
+            seg = s;
+            seg_begin = cu_seqlens[s];
+            kept = (size_t)slots[s] * (TAPS - 1);
+        }
+        const int local = t - seg_begin;
+        if (fresh) {
+#pragma unroll
+            for (int j = 0; j < TAPS - 1; ++j) {
+                const int back = TAPS - 1 - j;
+                if (local - back >= 0) win[j] = ss_load4(in, dtype, (size_t)(t - back) * ld + c);
+                else win[j] = ss_load4(tail, dtype, (kept + (TAPS - 1 + local - back)) * channels + c);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < TAPS - 1; ++j) win[j] = win[j + 1];
+        }
+        win[TAPS - 1] = ss_load4(in, dtype, (size_t)t * ld + c);
+        float4 acc = bias;
+#pragma unroll
+        for (int j = 0; j < TAPS; ++j) {
+            acc.x = fmaf(w[0][j], win[j].x, acc.x);
+            acc.y = fmaf(w[1][j], win[j].y, acc.y);
+            acc.z = fmaf(w[2][j], win[j].z, acc.z);
+            acc.w = fmaf(w[3][j], win[j].w, acc.w);
+        }
+        ss_store4(out, dtype, (size_t)t * channels + c, make_float4(ss_silu(acc.x), ss_silu(acc.y), ss_silu(acc.z), ss_silu(acc.w)));
+    }
+}
+
 // ---------------------------------------------------------------- the recurrence
 struct SsScanArgs {
     const void* u;            // [T, channels] after convolution and silu: x | B | C
@@ -453,6 +511,338 @@ ss_scan_packed_kernel(const SsScanArgs a) {
     if (last_part && a.write_state) ss_keep_inputs(a, head, group, seg_start, seg_len, slot, tid);
 }
 
+// ---------------------------------------------------------------- long segments on the tensor cores
+// A part of SSM_PART tokens that starts from the state S0, with l_i the sum of the logarithms of the decays up to and
+// including token i (l_i <= 0, float32):
+//   y_i   = exp(l_i) S0^T C_i + sum_(j<=i) (C_i . B_j) exp(l_i - l_j) dt_j x_j + D x_i
+//   S_end = exp(l_last) S0 + sum_j exp(l_last - l_j) dt_j B_j x_j^T
+// Only differences l_i - l_j <= 0 are exponentiated, so nothing overflows however fast a head forgets. x, B and C are
+// the bfloat16 numbers that left the convolution and enter their products as they are; what carries a step size, a
+// decay or the state is float32 and enters its product as a sum of two bfloat16 numbers (v = hi + lo, hi = bf16(v),
+// lo = bf16(v - hi): sixteen bits of mantissa), each half with a product of its own, sums in float32. Three launches:
+// every part's end state from zero (B'^T X); the parts' start states (stored as their two halves) and the segment's
+// last state, element by element; then every part's outputs (G = C B^T, Y1 = C S0, M = G * decays, Y2 = M X). A block
+// per (head, segment, part); rows past the segment's end are zero. Rows in shared memory are padded by 16 bytes so
+// that a fragment's rows fall into different banks; buffers whose contents are dead take the next phase's results.
+#include <mma.h>
+using namespace nvcuda;
+#define SSM_PART 64
+#define SSM_THREADS 256
+
+struct SsmLayout {
+    int ldn, ldp, ldm, ldg, ldy;                       // elements: bfloat16 rows of N, P and SSM_PART; float32 rows of G and Y
+    size_t c, b, x, s_hi, s_lo, g, meta, total, ends_total;
+};
+static __host__ __device__ inline size_t ssm_max(size_t a, size_t b) { return a > b ? a : b; }
+static __host__ __device__ inline SsmLayout ssm_layout(int P, int N) {
+    SsmLayout L;
+    L.ldn = N + 8; L.ldp = P + 8; L.ldm = SSM_PART + 8; L.ldg = SSM_PART + 4; L.ldy = P + 4;
+    size_t o = 0;
+    L.c = o; o += (size_t)SSM_PART * L.ldn * 2;                                   // C (outputs); low halves of B' (end states)
+    L.b = o; o += ssm_max((size_t)SSM_PART * L.ldn * 2, (size_t)SSM_PART * L.ldy * 4);   // B, then Y1; high halves of B'
+    L.x = o; o += (size_t)SSM_PART * L.ldp * 2;
+    L.meta = o; o += 4 * SSM_PART * sizeof(float);                                // dt, l, a warp's total
+    L.ends_total = o;
+    const size_t half = ssm_max((size_t)N * L.ldp * 2, (size_t)SSM_PART * L.ldm * 2);
+    L.s_hi = o; o += half;                                                        // S0's halves, then M's
+    L.s_lo = o; o += half;
+    L.g = o; o += ssm_max((size_t)SSM_PART * L.ldg * 4, (size_t)SSM_PART * L.ldy * 4);   // G, then Y2
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ void ssm_split(float v, __nv_bfloat16& hi, __nv_bfloat16& lo) {
+    hi = __float2bfloat16_rn(v);
+    lo = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+__device__ __forceinline__ void ssm_copy16(void* dst_shared, const void* src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst_shared);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void ssm_copies_done() {
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// dts[k] = softplus(dt_k + bias) and logs[k] = -rate (dt_0 + .. + dt_k) for the part's tokens; zero steps past its end
+__device__ __forceinline__ void ssm_steps(const SsScanArgs& a, int head, int t0, int nt, float* dts, float* logs, float* total) {
+    const int tid = threadIdx.x;
+    const float rate = a.rate[head], bias = a.dt_bias[head];
+    if (tid < SSM_PART) {                                                // two whole warps
+        float dt = 0.f;
+        if (tid < nt) dt = ss_softplus(ss_load(a.proj, a.dtype, (size_t)(t0 + tid) * a.ld + a.dt_off + head) + bias);
+        float sum = dt;
+#pragma unroll
+        for (int off = 1; off < 32; off *= 2) {
+            const float below = __shfl_up_sync(0xffffffffu, sum, off);
+            if ((tid & 31) >= off) sum += below;
+        }
+        if (tid == 31) total[0] = sum;
+        dts[tid] = dt;
+        logs[tid] = sum;
+    }
+    __syncthreads();
+    if (tid < SSM_PART) logs[tid] = -rate * (tid >= 32 ? logs[tid] + total[0] : logs[tid]);
+    __syncthreads();
+}
+
+// rows [SSM_PART, cols] of bfloat16 from u (row stride a.channels) into shared memory rows of ld elements, sixteen
+// bytes a copy, all in flight at once; rows past nt are zeroed
+__device__ __forceinline__ void ssm_copy_rows(const SsScanArgs& a, int t0, int nt, int col0, int cols, __nv_bfloat16* dst, int ld) {
+    const __nv_bfloat16* u = reinterpret_cast<const __nv_bfloat16*>(a.u);
+    const int chunks = cols / 8;
+    for (int i = threadIdx.x; i < SSM_PART * chunks; i += blockDim.x) {
+        const int k = i / chunks, c = (i - k * chunks) * 8;
+        if (k < nt) ssm_copy16(dst + (size_t)k * ld + c, u + (size_t)(t0 + k) * a.channels + col0 + c);
+        else *reinterpret_cast<uint4*>(dst + (size_t)k * ld + c) = make_uint4(0u, 0u, 0u, 0u);
+    }
+}
+
+__global__ void __launch_bounds__(SSM_THREADS)
+ss_part_ends_mma_kernel(const SsScanArgs a) {
+    extern __shared__ __align__(128) unsigned char ssm_smem[];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int head = blockIdx.x, seg = blockIdx.y, part = blockIdx.z;
+    const int P = a.P, N = a.N;
+    const int seg_start = a.cu_seqlens[seg], seg_len = a.cu_seqlens[seg + 1] - seg_start;
+    const int parts_here = max(1, (seg_len + SSM_PART - 1) / SSM_PART);
+    if (part >= parts_here || seg_len <= 0) return;
+    const int t0 = seg_start + part * SSM_PART, nt = min(SSM_PART, seg_start + seg_len - t0);
+    const SsmLayout L = ssm_layout(P, N);
+    __nv_bfloat16* Bl = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.c);
+    __nv_bfloat16* Bh = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.b);
+    __nv_bfloat16* Xs = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.x);
+    float* dts = reinterpret_cast<float*>(ssm_smem + L.meta);
+    float* logs = dts + SSM_PART;
+    const int tid = threadIdx.x, warp = tid / 32, warps = blockDim.x / 32;
+    const int inner = a.heads * P, group = head / (a.heads / a.groups);
+    ssm_copy_rows(a, t0, nt, head * P, P, Xs, L.ldp);
+    ssm_copy_rows(a, t0, nt, inner + group * N, N, Bh, L.ldn);           // B as it is; scaled in place below
+    ssm_steps(a, head, t0, nt, dts, logs, logs + SSM_PART);              // while the copies fly
+    ssm_copies_done();
+    __syncthreads();
+    const float l_last = logs[nt - 1];
+    for (int i = tid; i < SSM_PART * (N / 2); i += blockDim.x) {         // B'_j = exp(l_last - l_j) dt_j B_j in two halves
+        const int k = i / (N / 2), n = (i - k * (N / 2)) * 2;
+        const float w = k < nt ? expf(l_last - logs[k]) * dts[k] : 0.f;
+        __nv_bfloat162* hi = reinterpret_cast<__nv_bfloat162*>(Bh + (size_t)k * L.ldn + n);
+        const float2 v = __bfloat1622float2(*hi);
+        __nv_bfloat16 h0, l0, h1, l1;
+        ssm_split(v.x * w, h0, l0);
+        ssm_split(v.y * w, h1, l1);
+        *hi = __halves2bfloat162(h0, h1);
+        *reinterpret_cast<__nv_bfloat162*>(Bl + (size_t)k * L.ldn + n) = __halves2bfloat162(l0, l1);
+    }
+    __syncthreads();
+    float* dst = a.part_state + (((size_t)seg * a.heads + head) * a.parts + part) * N * P;
+    const int tiles_p = P / 16, tiles = (N / 16) * tiles_p;
+    for (int tile = warp; tile < tiles; tile += warps) {
+        const int ti = tile / tiles_p, tj = tile - ti * tiles_p;
+        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+        wmma::fill_fragment(acc, 0.f);
+#pragma unroll
+        for (int kk = 0; kk < SSM_PART / 16; ++kk) {
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::col_major> fa;    // B'^T: element (n, j) = B'[j][n]
+            wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> fb;
+            wmma::load_matrix_sync(fb, Xs + (size_t)kk * 16 * L.ldp + tj * 16, L.ldp);
+            wmma::load_matrix_sync(fa, Bh + (size_t)kk * 16 * L.ldn + ti * 16, L.ldn);
+            wmma::mma_sync(acc, fa, fb, acc);
+            wmma::load_matrix_sync(fa, Bl + (size_t)kk * 16 * L.ldn + ti * 16, L.ldn);
+            wmma::mma_sync(acc, fa, fb, acc);
+        }
+        wmma::store_matrix_sync(dst + (size_t)ti * 16 * P + tj * 16, acc, P, wmma::mem_row_major);
+    }
+    if (tid == 0) a.part_log[((size_t)seg * a.heads + head) * a.parts + part] = l_last;
+}
+
+// Element by element over a segment's parts: start_0 = the request's state, start_(k+1) = exp(l_k) start_k + E_k. The
+// start states go to `starts` as their two bfloat16 halves ([.., part, half, N P]); the state after the last part goes
+// to the request's slot.
+__global__ void __launch_bounds__(256)
+ss_prefix_all_kernel(float* __restrict__ state, const int* __restrict__ cu_seqlens, const int* __restrict__ slots,
+                     const float* __restrict__ part_state, __nv_bfloat16* __restrict__ starts, const float* __restrict__ part_log,
+                     int heads, int elems, int parts, int write_state) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const int head = blockIdx.x, seg = blockIdx.y;
+    const int seg_len = cu_seqlens[seg + 1] - cu_seqlens[seg];
+    if (seg_len <= 0) return;
+    const int parts_here = (seg_len + SSM_PART - 1) / SSM_PART;
+    float* s0 = state + ((size_t)slots[seg] * heads + head) * elems;
+    const float* ps = part_state + ((size_t)seg * heads + head) * parts * elems;
+    __nv_bfloat16* st = starts + ((size_t)seg * heads + head) * parts * elems * 2;
+    const float* pl = part_log + ((size_t)seg * heads + head) * parts;
+    for (int i = 2 * (blockIdx.z * blockDim.x + threadIdx.x); i < elems; i += 2 * gridDim.z * blockDim.x) {   // elems is even
+        float2 s = *reinterpret_cast<const float2*>(s0 + i);
+        for (int k0 = 0; k0 < parts_here; k0 += 8) {                     // eight parts' loads in flight ahead of the chain
+            float2 e[8];
+            float d[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const bool have = k0 + j < parts_here;
+                e[j] = have ? *reinterpret_cast<const float2*>(ps + (size_t)(k0 + j) * elems + i) : make_float2(0.f, 0.f);
+                d[j] = have ? expf(pl[k0 + j]) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                if (k0 + j < parts_here) {
+                    __nv_bfloat16 hx, lx, hy, ly;
+                    ssm_split(s.x, hx, lx);
+                    ssm_split(s.y, hy, ly);
+                    *reinterpret_cast<__nv_bfloat162*>(st + (size_t)(k0 + j) * 2 * elems + i) = __halves2bfloat162(hx, hy);
+                    *reinterpret_cast<__nv_bfloat162*>(st + (size_t)(k0 + j) * 2 * elems + elems + i) = __halves2bfloat162(lx, ly);
+                    s.x = fmaf(d[j], s.x, e[j].x);
+                    s.y = fmaf(d[j], s.y, e[j].y);
+                }
+            }
+        }
+        if (write_state) *reinterpret_cast<float2*>(s0 + i) = s;
+    }
+}
+
+__global__ void __launch_bounds__(SSM_THREADS, 2)
+ss_part_out_mma_kernel(const SsScanArgs a, const __nv_bfloat16* __restrict__ starts) {
+    extern __shared__ __align__(128) unsigned char ssm_smem[];
+    pdl_wait();
+    pdl_launch_dependents();
+    const int head = blockIdx.x, seg = blockIdx.y, part = blockIdx.z;
+    const int P = a.P, N = a.N;
+    const int seg_start = a.cu_seqlens[seg], seg_len = a.cu_seqlens[seg + 1] - seg_start;
+    const int parts_here = max(1, (seg_len + SSM_PART - 1) / SSM_PART);
+    if (part >= parts_here || seg_len <= 0) return;
+    const int t0 = seg_start + part * SSM_PART, nt = min(SSM_PART, seg_start + seg_len - t0);
+    const SsmLayout L = ssm_layout(P, N);
+    __nv_bfloat16* Cs = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.c);
+    __nv_bfloat16* Bs = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.b);
+    float* Y1 = reinterpret_cast<float*>(ssm_smem + L.b);                 // once G is done
+    __nv_bfloat16* Xs = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.x);
+    __nv_bfloat16* Sh = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.s_hi);
+    __nv_bfloat16* Sl = reinterpret_cast<__nv_bfloat16*>(ssm_smem + L.s_lo);
+    __nv_bfloat16* Mh = Sh;                                              // once Y1 is done
+    __nv_bfloat16* Ml = Sl;
+    float* G = reinterpret_cast<float*>(ssm_smem + L.g);
+    float* Y2 = G;                                                       // once M is done
+    float* dts = reinterpret_cast<float*>(ssm_smem + L.meta);
+    float* logs = dts + SSM_PART;
+    const int tid = threadIdx.x, warp = tid / 32, warps = blockDim.x / 32;
+    const int inner = a.heads * P, group = head / (a.heads / a.groups);
+    ssm_copy_rows(a, t0, nt, inner + group * N, N, Bs, L.ldn);
+    ssm_copy_rows(a, t0, nt, inner + (a.groups + group) * N, N, Cs, L.ldn);
+    ssm_copy_rows(a, t0, nt, head * P, P, Xs, L.ldp);
+    {   // the part's start state, stored as its two halves
+        const __nv_bfloat16* src = starts + (((size_t)seg * a.heads + head) * a.parts + part) * 2 * N * P;
+        const int chunks = P / 8;
+        for (int i = tid; i < N * chunks; i += blockDim.x) {
+            const int n = i / chunks, c = (i - n * chunks) * 8;
+            ssm_copy16(Sh + (size_t)n * L.ldp + c, src + (size_t)n * P + c);
+            ssm_copy16(Sl + (size_t)n * L.ldp + c, src + (size_t)(N + n) * P + c);
+        }
+    }
+    ssm_steps(a, head, t0, nt, dts, logs, logs + SSM_PART);              // while the copies fly
+    ssm_copies_done();
+    __syncthreads();
+    const int tiles_p = P / 16, rows = SSM_PART / 16;
+    for (int tile = warp; tile < rows * (rows + 1) / 2; tile += warps) { // G = C B^T, on and below its diagonal
+        int ti = 0, first = 0;
+        while (first + ti + 1 <= tile) { first += ti + 1; ++ti; }
+        const int tj = tile - first;
+        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+        wmma::fill_fragment(acc, 0.f);
+        for (int kk = 0; kk < N / 16; ++kk) {
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> fa;
+            wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::col_major> fb;    // B^T: element (n, j) = B[j][n]
+            wmma::load_matrix_sync(fa, Cs + (size_t)ti * 16 * L.ldn + kk * 16, L.ldn);
+            wmma::load_matrix_sync(fb, Bs + (size_t)tj * 16 * L.ldn + kk * 16, L.ldn);
+            wmma::mma_sync(acc, fa, fb, acc);
+        }
+        wmma::store_matrix_sync(G + ti * 16 * L.ldg + tj * 16, acc, L.ldg, wmma::mem_row_major);
+    }
+    __syncthreads();                                                     // B is read; its place takes Y1
+    for (int tile = warp; tile < rows * tiles_p; tile += warps) {        // Y1 = C S0
+        const int ti = tile / tiles_p, tj = tile - ti * tiles_p;
+        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+        wmma::fill_fragment(acc, 0.f);
+        for (int kk = 0; kk < N / 16; ++kk) {
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> fa;
+            wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> fb;
+            wmma::load_matrix_sync(fa, Cs + (size_t)ti * 16 * L.ldn + kk * 16, L.ldn);
+            wmma::load_matrix_sync(fb, Sh + (size_t)kk * 16 * L.ldp + tj * 16, L.ldp);
+            wmma::mma_sync(acc, fa, fb, acc);
+            wmma::load_matrix_sync(fb, Sl + (size_t)kk * 16 * L.ldp + tj * 16, L.ldp);
+            wmma::mma_sync(acc, fa, fb, acc);
+        }
+        wmma::store_matrix_sync(Y1 + (size_t)ti * 16 * L.ldy + tj * 16, acc, L.ldy, wmma::mem_row_major);
+    }
+    __syncthreads();                                                     // S0 is read; its place takes M
+    // M_ij = G_ij exp(l_i - l_j) dt_j for j <= i inside the part, zero elsewhere; in two halves
+    for (int idx = tid; idx < SSM_PART * SSM_PART; idx += blockDim.x) {
+        const int i = idx / SSM_PART, j = idx - i * SSM_PART;
+        float v = 0.f;
+        if (j <= i && i < nt) v = G[i * L.ldg + j] * expf(logs[i] - logs[j]) * dts[j];
+        ssm_split(v, Mh[i * L.ldm + j], Ml[i * L.ldm + j]);
+    }
+    __syncthreads();                                                     // G is read; its place takes Y2
+    for (int tile = warp; tile < rows * tiles_p; tile += warps) {        // Y2 = M X
+        const int ti = tile / tiles_p, tj = tile - ti * tiles_p;
+        wmma::fragment<wmma::accumulator, 16, 16, 16, float> acc;
+        wmma::fill_fragment(acc, 0.f);
+        for (int kk = 0; kk <= ti; ++kk) {                               // M is zero right of its diagonal
+            wmma::fragment<wmma::matrix_a, 16, 16, 16, __nv_bfloat16, wmma::row_major> fa;
+            wmma::fragment<wmma::matrix_b, 16, 16, 16, __nv_bfloat16, wmma::row_major> fb;
+            wmma::load_matrix_sync(fb, Xs + (size_t)kk * 16 * L.ldp + tj * 16, L.ldp);
+            wmma::load_matrix_sync(fa, Mh + ti * 16 * L.ldm + kk * 16, L.ldm);
+            wmma::mma_sync(acc, fa, fb, acc);
+            wmma::load_matrix_sync(fa, Ml + ti * 16 * L.ldm + kk * 16, L.ldm);
+            wmma::mma_sync(acc, fa, fb, acc);
+        }
+        wmma::store_matrix_sync(Y2 + (size_t)ti * 16 * L.ldy + tj * 16, acc, L.ldy, wmma::mem_row_major);
+    }
+    __syncthreads();
+    const float skip = a.skip[head];
+    const int quads = P / 4;
+    for (int idx = tid; idx < nt * quads; idx += blockDim.x) {
+        const int i = idx / quads, p = (idx - i * quads) * 4;
+        const float decayed = expf(logs[i]);
+        const float4 y1 = *reinterpret_cast<const float4*>(Y1 + (size_t)i * L.ldy + p);
+        const float4 y2 = *reinterpret_cast<const float4*>(Y2 + (size_t)i * L.ldy + p);
+        const __nv_bfloat16* x = Xs + (size_t)i * L.ldp + p;
+        *reinterpret_cast<float4*>(a.y + (size_t)(t0 + i) * inner + head * P + p) =
+            make_float4(fmaf(decayed, y1.x, y2.x) + skip * __bfloat162float(x[0]),
+                        fmaf(decayed, y1.y, y2.y) + skip * __bfloat162float(x[1]),
+                        fmaf(decayed, y1.z, y2.z) + skip * __bfloat162float(x[2]),
+                        fmaf(decayed, y1.w, y2.w) + skip * __bfloat162float(x[3]));
+    }
+    if (part == parts_here - 1 && a.write_state) ss_keep_inputs(a, head, group, seg_start, seg_len, a.slots[seg], tid);
+}
+
+// Sizes and buffers the tensor-core form takes: bfloat16 activations, parts of SSM_PART tokens, head sizes in whole
+// fragments, rows on 16-byte boundaries. part_state then holds twice segments * heads * parts * N * P floats: the
+// parts' end states and, behind them, their start states in halves.
+static int ssm_supported(const SsScanArgs& a, int dtype) {
+    if (dtype != TTB_DTYPE_BF16 || a.parts < 2 || a.part_len != SSM_PART) return 0;
+    if (a.P % 16 || a.N % 16 || a.channels % 8) return 0;
+    if (ssm_layout(a.P, a.N).total > 200 * 1024) return 0;
+    return (uintptr_t)a.u % 16 == 0 && (uintptr_t)a.y % 16 == 0 && (uintptr_t)a.part_state % 32 == 0 && (uintptr_t)a.state % 16 == 0;
+}
+
+static void ssm_launch(const SsScanArgs& a, int segments, cudaStream_t stream) {
+    const SsmLayout L = ssm_layout(a.P, a.N);
+    static TtbOncePerDevice once;
+    if (once.pending()) {
+        cudaFuncSetAttribute(ss_part_ends_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(ss_part_out_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        once.mark();
+    }
+    const dim3 grid(a.heads, segments, a.parts);
+    const int elems = a.N * a.P;
+    __nv_bfloat16* starts = reinterpret_cast<__nv_bfloat16*>(a.part_state + (size_t)segments * a.heads * a.parts * elems);
+    ttb_launch(ss_part_ends_mma_kernel, grid, SSM_THREADS, L.ends_total, stream, a);
+    ttb_launch(ss_prefix_all_kernel, dim3(a.heads, segments, (elems / 2 + 255) / 256), 256, 0, stream, a.state, a.cu_seqlens, a.slots,
+               (const float*)a.part_state, starts, (const float*)a.part_log, a.heads, elems, a.parts, a.write_state);
+    ttb_launch(ss_part_out_mma_kernel, grid, SSM_THREADS, L.total, stream, a, (const __nv_bfloat16*)starts);
+}
+
 // start_(k+1) = exp(L_k) start_k + E_k over the parts of a segment, element by element; E_k's place takes start_(k+1)
 __global__ void __launch_bounds__(256)
 ss_prefix_kernel(const float* __restrict__ state, const int* __restrict__ cu_seqlens, const int* __restrict__ slots,
@@ -546,7 +936,18 @@ TTB_EXPORT int ttb_conv_silu(const void* in, int dtype, int ld, const float* con
                        (uintptr_t)conv_b % 16 == 0 && (taps == 1 || (uintptr_t)tail % unit == 0);
     const size_t total = (size_t)tokens * channels;
     const int blocks = (int)((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
-    if (quads)
+    if (quads && tokens >= 64 * SS_CONV_RUN && taps >= 2 && taps <= 4) {
+        const dim3 grid((tokens + SS_CONV_RUN - 1) / SS_CONV_RUN, (channels / 4 + 127) / 128);
+        if (taps == 2)
+            ttb_launch(ss_conv_silu_run_kernel<2>, grid, 128, 0, stream, in, dtype, ld, conv_w, conv_b, seg_of_token, cu_seqlens,
+                       slots, tail, out, tokens, channels);
+        else if (taps == 3)
+            ttb_launch(ss_conv_silu_run_kernel<3>, grid, 128, 0, stream, in, dtype, ld, conv_w, conv_b, seg_of_token, cu_seqlens,
+                       slots, tail, out, tokens, channels);
+        else
+            ttb_launch(ss_conv_silu_run_kernel<4>, grid, 128, 0, stream, in, dtype, ld, conv_w, conv_b, seg_of_token, cu_seqlens,
+                       slots, tail, out, tokens, channels);
+    } else if (quads)
         ttb_launch(ss_conv_silu4_kernel, tokens < 148 * 16 ? tokens : 148 * 16, channels / 4 >= 256 ? 256 : 128, 0, stream, in,
                    dtype, ld, conv_w, conv_b, seg_of_token, cu_seqlens, slots, tail, out, tokens, channels, taps);
     else
@@ -613,6 +1014,10 @@ TTB_EXPORT int ttb_state_space_scan(const void* u, const void* proj, int dtype, 
             default: ss_scan_packed_launch<32>(a, segments, threads, packed_smem, ENDS, stream); break;        \
         }                                                                                                      \
     } while (0)
+    if (ssm_supported(a, dtype)) {
+        ssm_launch(a, segments, stream);
+        return ttb_launch_status();
+    }
     if (parts > 1) {
         if (packed) SS_PACKED(true);
         else SS_PICK(true);
@@ -631,6 +1036,7 @@ TTB_EXPORT int ttb_state_space_scan(const void* u, const void* proj, int dtype, 
 
 // ---------------------------------------------------------------- gate, then the RMS norm in equal parts
 // out[t, c] = v / sqrt(mean_part(v^2) + eps) * w[c], v = y[t, c] * silu(z[t, c]); a block per (token, part).
+#define SS_GATE_KEEP 8
 __global__ void __launch_bounds__(128)
 ss_gate_norm_kernel(const float* __restrict__ y, const void* __restrict__ z, int z_dtype, int z_stride,
                     const float* __restrict__ weight, float eps, void* __restrict__ out, int out_dtype, int inner, int part) {
@@ -638,14 +1044,28 @@ ss_gate_norm_kernel(const float* __restrict__ y, const void* __restrict__ z, int
     pdl_wait();
     pdl_launch_dependents();
     const int t = blockIdx.x, c0 = blockIdx.y * part;
+    // a thread's first SS_GATE_KEEP values stay in registers between the sum and the scaling; wider parts read the rest twice
+    float kept[SS_GATE_KEEP];
     float sumsq = 0.f;
-    for (int c = threadIdx.x; c < part; c += blockDim.x) {
+#pragma unroll
+    for (int j = 0; j < SS_GATE_KEEP; ++j) {
+        const int c = threadIdx.x + j * blockDim.x;
+        kept[j] = 0.f;
+        if (c < part) kept[j] = y[(size_t)t * inner + c0 + c] * ss_silu(ss_load(z, z_dtype, (size_t)t * z_stride + c0 + c));
+        sumsq += kept[j] * kept[j];
+    }
+    for (int c = threadIdx.x + SS_GATE_KEEP * blockDim.x; c < part; c += blockDim.x) {
         const float v = y[(size_t)t * inner + c0 + c] * ss_silu(ss_load(z, z_dtype, (size_t)t * z_stride + c0 + c));
         sumsq += v * v;
     }
     sumsq = block_sum(sumsq, scratch);
     const float scale = 1.f / sqrtf(sumsq / (float)part + eps);
-    for (int c = threadIdx.x; c < part; c += blockDim.x) {
+#pragma unroll
+    for (int j = 0; j < SS_GATE_KEEP; ++j) {
+        const int c = threadIdx.x + j * blockDim.x;
+        if (c < part) ss_store(out, out_dtype, (size_t)t * inner + c0 + c, kept[j] * scale * weight[c0 + c]);
+    }
+    for (int c = threadIdx.x + SS_GATE_KEEP * blockDim.x; c < part; c += blockDim.x) {
         const float v = y[(size_t)t * inner + c0 + c] * ss_silu(ss_load(z, z_dtype, (size_t)t * z_stride + c0 + c));
         ss_store(out, out_dtype, (size_t)t * inner + c0 + c, v * scale * weight[c0 + c]);
     }

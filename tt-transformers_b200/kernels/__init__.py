@@ -1324,7 +1324,8 @@ class CudaKernels:
                 part_len *= 2
             parts = -(-batch.max_seg_len // part_len)
         if parts > 1:
-            part_state = torch.empty(batch.num_segments * heads * parts * state * vdim, dtype=torch.float32, device=self.device)
+            # the parts' end states and, behind them, room for their start states
+            part_state = torch.empty(2 * batch.num_segments * heads * parts * state * vdim, dtype=torch.float32, device=self.device)
             part_log = torch.empty(batch.num_segments * heads * parts, dtype=torch.float32, device=self.device)
             self.launches += 2
         y = torch.empty(T, inner, dtype=torch.float32, device=self.device)
