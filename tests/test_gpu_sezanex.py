@@ -168,6 +168,44 @@ def test_state_space_against_its_twin(kernels, twin, dtype, H, P, N, G, R, taps,
         segs = [(p + n, m) for (p, n), m in zip(segs, (1, 3, 1, 200, 2, 1, 64))]
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,P,N,G,R,taps", [(4, 16, 24, 2, 1, 4), (8, 64, 128, 2, 4, 4), (6, 32, 16, 3, 2, 3), (1, 4, 1, 1, 1, 1),
+                                            (4, 128, 64, 1, 4, 2), (6, 7, 3, 2, 2, 2), (12, 8, 40, 4, 3, 5), (2, 1024, 8, 2, 1, 4)])
+def test_state_space_decode_steps_against_their_twin(kernels, twin, dtype, H, P, N, G, R, taps):
+    """Steps of one token a request (the walk, the gate and the group norm as one launch where the sizes allow), five in
+    a row on slots in any order, each from what the one before left; a step that must only read leaves state and kept
+    inputs as they were; the counters the launch uses are zero again after it."""
+    g = torch.Generator().manual_seed(3 * H + P + N)
+    slots = [6, 0, 3, 1, 8, 4]
+    inner, GN = H * P, G * N
+    C = inner + 2 * GN
+    conv_w, conv_b = (0.5 * torch.randn(C, taps, generator=g)).to(DEV), (0.2 * torch.randn(C, generator=g)).to(DEV)
+    dt_bias = (torch.randn(H, generator=g) - 0.5).to(DEV)
+    rate = torch.exp(torch.rand(H, generator=g) * 4 - 3).to(DEV)
+    skip, norm_w = torch.randn(H, generator=g).to(DEV), (1 + 0.3 * torch.randn(inner, generator=g)).to(DEV)
+    state = (torch.randn(10, H, N, P, generator=g) * 0.5).to(DEV)
+    tail = torch.randn(10, max(taps - 1, 1), C, generator=g).to(DEV, dtype)
+    for step in range(5):
+        batch = _batch([(40 + step, 1)] * len(slots), slots)
+        proj = torch.randn(batch.num_tokens, 2 * inner + 2 * GN + H, generator=g).to(DEV, dtype)
+        views = [MatrixState(H, N, P, C, taps).view({"state": state.clone(), "tail": tail.clone()}, slots=batch.seg_slot,
+                                                    slot_list=slots) for _ in range(2)]
+        ref = twin.state_space(proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, 1e-5, H, P, N, G, R, batch, views[0])
+        got = kernels.state_space(proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, 1e-5, H, P, N, G, R, batch, views[1])
+        _close(got, ref, 1e-4 if dtype == torch.float32 else 2e-2)
+        _close(views[1].state, views[0].state, 1e-4 if dtype == torch.float32 else 2e-3)
+        if taps > 1:
+            assert torch.equal(views[1].tail, views[0].tail)
+        assert torch.equal(views[1].state[[2, 5, 7, 9]], state[[2, 5, 7, 9]])
+        kept_state, kept_tail = views[1].state.clone(), views[1].tail.clone()
+        again = kernels.state_space(proj, conv_w, conv_b, dt_bias, rate, skip, norm_w, 1e-5, H, P, N, G, R, batch, views[1],
+                                    write_state=False)
+        assert torch.equal(views[1].state, kept_state) and torch.equal(views[1].tail, kept_tail)
+        counter = getattr(kernels, "_ss_counter", None)
+        assert counter is None or not bool(counter.any())
+        state, tail = views[1].state, views[1].tail
+
+
 @pytest.mark.parametrize("H,P,N,G,taps", [(4, 64, 128, 2, 4), (2, 32, 64, 1, 3), (3, 16, 16, 3, 2), (2, 128, 32, 2, 4)])
 @pytest.mark.parametrize("decay", [1.0, 40.0])
 def test_state_space_on_tensor_cores_keeps_float32_where_the_walk_does(kernels, H, P, N, G, taps, decay):

@@ -1079,3 +1079,142 @@ TTB_EXPORT int ttb_gate_group_norm(const float* y, const void* z, int z_dtype, i
                inner, inner / parts);
     return ttb_launch_status();
 }
+
+// ---------------------------------------------------------------- decode steps: one token a segment
+// The walk of one token, the gate and the group norm in one launch. A block per (head, segment): the head's state is read,
+// decayed, updated and written once (four columns a thread, row groups side by side, their partial outputs summed in a
+// fixed order), v = (S^T C + D x) silu(z) goes to `gated` in float32 and the head's sum of v^2 to `partial`. The block that
+// is the last of its norm group to finish (a counter per segment and norm group; it leaves the counter at zero for the
+// next step) sums the group's partial sums in head order and writes the normed values. Nobody waits for anybody.
+// A norm group holds whole heads: heads is a multiple of norm_groups.
+struct SsTokenArgs {
+    SsScanArgs s;             // u, proj, offsets, per-head vectors, segments' slots, the state, kept inputs; y = `gated`
+    const float* norm_w;      // [heads * P]
+    void* out;                // [segments, heads * P], the compute dtype
+    float* partial;           // [segments, heads]
+    int* counter;             // [segments, norm_groups], zero between launches
+    float eps;
+    int norm_groups;
+};
+
+__global__ void __launch_bounds__(256)
+ss_token_kernel(const SsTokenArgs g) {
+    extern __shared__ __align__(16) float sst_smem[];
+    __shared__ float scratch[32];
+    __shared__ int is_last;
+    pdl_wait();
+    pdl_launch_dependents();
+    const SsScanArgs& a = g.s;
+    const int head = blockIdx.x, seg = blockIdx.y;
+    const int P = a.P, N = a.N;
+    const int t = a.cu_seqlens[seg];
+    if (a.cu_seqlens[seg + 1] - t != 1) return;
+    const int tid = threadIdx.x;
+    const int inner = a.heads * P, group = head / (a.heads / a.groups);
+    const int cols = P / 4, row_groups = min(blockDim.x / cols, N);
+    float* xs = sst_smem;                                    // [P]
+    float* bs = xs + P;                                      // [N]  dt B
+    float* cs = bs + N;                                      // [N]
+    float* ypart = sst_smem + ((P + 2 * N + 3) & ~3);        // [row_groups, P], on a 16-byte boundary
+    const int slot = a.slots[seg];
+    const float dt = ss_softplus(ss_load(a.proj, a.dtype, (size_t)t * a.ld + a.dt_off + head) + a.dt_bias[head]);
+    const float decay = expf(-a.rate[head] * dt);
+    const size_t row = (size_t)t * a.channels;
+    for (int p = tid; p < P; p += blockDim.x) xs[p] = ss_load(a.u, a.dtype, row + head * P + p);
+    for (int n = tid; n < N; n += blockDim.x) {
+        bs[n] = dt * ss_load(a.u, a.dtype, row + inner + group * N + n);
+        cs[n] = ss_load(a.u, a.dtype, row + inner + (a.groups + group) * N + n);
+    }
+    __syncthreads();
+    const int col = tid % cols, rg = tid / cols;
+    if (rg < row_groups) {
+        float* S = a.state + ((size_t)slot * a.heads + head) * N * P + col * 4;
+        const float4 x = *reinterpret_cast<const float4*>(xs + col * 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int n0 = rg; n0 < N; n0 += 4 * row_groups) {                // four rows' loads in flight
+            float4 s[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + j * row_groups;
+                if (n < N) s[j] = *reinterpret_cast<const float4*>(S + (size_t)n * P);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int n = n0 + j * row_groups;
+                if (n < N) {
+                    const float b = bs[n], c = cs[n];
+                    s[j].x = fmaf(decay, s[j].x, b * x.x); s[j].y = fmaf(decay, s[j].y, b * x.y);
+                    s[j].z = fmaf(decay, s[j].z, b * x.z); s[j].w = fmaf(decay, s[j].w, b * x.w);
+                    acc.x = fmaf(s[j].x, c, acc.x); acc.y = fmaf(s[j].y, c, acc.y);
+                    acc.z = fmaf(s[j].z, c, acc.z); acc.w = fmaf(s[j].w, c, acc.w);
+                    if (a.write_state) *reinterpret_cast<float4*>(S + (size_t)n * P) = s[j];
+                }
+            }
+        }
+        *reinterpret_cast<float4*>(ypart + (size_t)rg * P + col * 4) = acc;
+    }
+    __syncthreads();
+    const float skip = a.skip[head];
+    float sumsq = 0.f;
+    for (int p = tid; p < P; p += blockDim.x) {
+        float y = 0.f;
+        for (int r = 0; r < row_groups; ++r) y += ypart[(size_t)r * P + p];
+        y = fmaf(skip, xs[p], y);
+        const float v = y * ss_silu(ss_load(a.proj, a.dtype, (size_t)t * a.ld + head * P + p));
+        a.y[(size_t)t * inner + head * P + p] = v;
+        sumsq += v * v;
+    }
+    sumsq = block_sum(sumsq, scratch);
+    const int heads_per = a.heads / g.norm_groups, ng = head / heads_per;
+    if (tid == 0) g.partial[(size_t)seg * a.heads + head] = sumsq;
+    __threadfence();                                                     // this block's values and sum before its count
+    __syncthreads();
+    if (tid == 0) {
+        const int before = atomicAdd(g.counter + (size_t)seg * g.norm_groups + ng, 1);
+        is_last = before == heads_per - 1;
+    }
+    __syncthreads();
+    if (a.write_state) ss_keep_inputs(a, head, group, t, 1, slot, tid);
+    if (!is_last) return;
+    __threadfence();
+    float total = 0.f;
+    for (int h = 0; h < heads_per; ++h) total += __ldcg(g.partial + (size_t)seg * a.heads + ng * heads_per + h);
+    const int part = heads_per * P;
+    const float scale = 1.f / sqrtf(total / (float)part + g.eps);
+    for (int c = tid; c < part; c += blockDim.x) {
+        const size_t i = (size_t)t * inner + (size_t)ng * part + c;
+        ss_store(g.out, a.dtype, i, __ldcg(a.y + i) * scale * g.norm_w[(size_t)ng * part + c]);
+    }
+    if (tid == 0) g.counter[(size_t)seg * g.norm_groups + ng] = 0;
+}
+
+// One decoded token per segment: u [segments, channels] after the convolution, proj [segments, z | x B C | dt] with row
+// stride ld, gated float32 [segments, heads P] (scratch), partial float32 [segments, heads], counter int32
+// [segments, norm_groups] holding zeros (and left so), out [segments, heads P] of the compute dtype.
+TTB_EXPORT int ttb_state_space_token(const void* u, const void* proj, int dtype, int ld, int conv_off, int dt_off,
+                                     const float* dt_bias, const float* rate, const float* skip, const int* cu_seqlens,
+                                     const int* slots, float* state, void* tail, float* gated, const float* norm_w, float eps,
+                                     void* out, float* partial, int* counter, int segments, int heads, int P, int N, int groups,
+                                     int norm_groups, int taps, int write_state, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!u || !proj || !dt_bias || !rate || !skip || !cu_seqlens || !slots || !state || !gated || !norm_w || !out || !partial ||
+        !counter || (taps > 1 && !tail))
+        return TTB_ERR_ARGUMENT;
+    if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    if (heads < 1 || groups < 1 || norm_groups < 1 || heads % groups || heads % norm_groups || P % 4 || P / 4 > 256 || N < 1 ||
+        (uintptr_t)state % 16)
+        return TTB_ERR_UNSUPPORTED;
+    const int row_groups = 256 / (P / 4) < N ? 256 / (P / 4) : N;
+    const size_t smem = ((size_t)((P + 2 * N + 3) & ~3) + (size_t)row_groups * P) * sizeof(float);
+    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    SsTokenArgs g;
+    SsScanArgs& a = g.s;
+    a.u = u; a.proj = proj; a.dtype = dtype; a.ld = ld; a.conv_off = conv_off; a.dt_off = dt_off;
+    a.dt_bias = dt_bias; a.rate = rate; a.skip = skip; a.cu_seqlens = cu_seqlens; a.slots = slots;
+    a.state = state; a.tail = tail; a.y = gated; a.part_state = nullptr; a.part_log = nullptr;
+    a.heads = heads; a.P = P; a.N = N; a.groups = groups; a.channels = heads * P + 2 * groups * N; a.taps = taps;
+    a.write_state = write_state; a.parts = 1; a.part_len = 1; a.NG = 1;
+    g.norm_w = norm_w; g.out = out; g.partial = partial; g.counter = counter; g.eps = eps; g.norm_groups = norm_groups;
+    ttb_launch(ss_token_kernel, dim3(heads, segments), 256, smem, stream, g);
+    return ttb_launch_status();
+}

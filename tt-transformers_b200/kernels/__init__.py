@@ -103,7 +103,7 @@ class CudaKernels:
                      "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports",
                      "ttb_recurrent_token", "ttb_add_dyntanh", "ttb_concat_cast", "ttb_qk_whole_norm_rope_write",
                      "ttb_route_top_scored", "ttb_moe_gemv_scaled", "ttb_gather_rows_scaled", "ttb_conv_silu",
-                     "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm"):
+                     "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm", "ttb_state_space_token"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -1315,6 +1315,22 @@ class CudaKernels:
         self._check(self.lib.ttb_conv_silu(self._p(xin), code, proj.stride(0), self._p(conv_w), self._p(conv_b),
                                            self._p(batch.seg_of_token), self._p(batch.cu_seqlens), self._p(view.slots),
                                            self._p(view.tail), self._p(u), T, C, taps, self._stream()), "conv_silu")
+        if (batch.max_seg_len == 1 and T == batch.num_segments and heads % norm_groups == 0 and vdim % 4 == 0 and vdim <= 1024
+                and (vdim + 2 * state + 3 + min(256 // max(vdim // 4, 1), state) * vdim) * 4 <= 48 * 1024):
+            # one token a segment: the walk, the gate and the group norm in one launch
+            counter = getattr(self, "_ss_counter", None)
+            if counter is None or counter.numel() < T * norm_groups:
+                counter = torch.zeros(max(T * norm_groups, 1 << 14), dtype=torch.int32, device=self.device)
+                self._ss_counter = counter                              # the kernel leaves it at zero
+            gated = torch.empty(T, inner, dtype=torch.float32, device=self.device)
+            partial = torch.empty(T, heads, dtype=torch.float32, device=self.device)
+            out = torch.empty(T, inner, dtype=proj.dtype, device=self.device)
+            self._check(self.lib.ttb_state_space_token(
+                self._p(u), self._p(proj), code, proj.stride(0), inner, inner + C, self._p(dt_bias), self._p(rate), self._p(skip),
+                self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(gated),
+                self._p(norm_w), ctypes.c_float(eps), self._p(out), self._p(partial), self._p(counter), batch.num_segments, heads,
+                vdim, state, groups, norm_groups, taps, 1 if write_state else 0, self._stream()), "state_space_token")
+            return out
         # long segments run as parts side by side (three launches: the parts' end states from zero, their start states,
         # the walk that writes out)
         part_len, parts, part_state, part_log = self.STATE_SPACE_PART, 1, None, None
