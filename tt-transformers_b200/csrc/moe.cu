@@ -20,7 +20,7 @@
 // TPB tokens a block: a row of W_r is read once for all of them (with many tokens the reads of W_r from L2 are
 // what the kernel waits for). A warp per logit row; then a warp per token selects.
 template <typename T, int TPB>
-__global__ void __launch_bounds__(TPB == 1 ? 1024 : 512)
+__global__ void __launch_bounds__(TPB == 1 ? 1024 : 512, TPB == 1 ? 1 : 2)       // many tokens: two blocks an SM
 route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
                  int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate,
                  int tokens, int scores) {
@@ -38,9 +38,30 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
     pdl_wait();
     pdl_launch_dependents();
     const int t0 = blockIdx.x * TPB, nt = min(TPB, tokens - t0);
-    for (int i = 0; i < TPB; ++i)
-        for (int c = threadIdx.x; c < wpad; c += blockDim.x)
-            h[i * wpad + c] = (i < nt && c < width) ? to_float(x[(size_t)(t0 + i) * ldx + c]) : 0.f;
+    if (TPB > 1 && (width & 3) == 0 && (ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & (4 * sizeof(T) - 1)) == 0) {
+        // four neighbouring values a load, every row's loads in flight together
+        const int quads = width / 4;
+        for (int q = threadIdx.x; q < TPB * quads; q += blockDim.x) {
+            const int i = q / quads, c = (q - i * quads) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < nt) {
+                const T* src = x + (size_t)(t0 + i) * ldx + c;
+                if constexpr (sizeof(T) == 2) {
+                    const uint2 raw = *reinterpret_cast<const uint2*>(src);
+                    const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+                    const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+                    v = make_float4(lo.x, lo.y, hi.x, hi.y);
+                } else {
+                    v = *reinterpret_cast<const float4*>(src);
+                }
+            }
+            *reinterpret_cast<float4*>(h + i * wpad + c) = v;
+        }
+    } else {
+        for (int i = 0; i < TPB; ++i)
+            for (int c = threadIdx.x; c < wpad; c += blockDim.x)
+                h[i * wpad + c] = (i < nt && c < width) ? to_float(x[(size_t)(t0 + i) * ldx + c]) : 0.f;
+    }
     for (int e = threadIdx.x; e < TPB * experts; e += blockDim.x) taken[e] = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
