@@ -315,6 +315,37 @@ def test_engine_matches_the_plain_implementation(tmp_path, dtype, tol, name):
             engine.close()
 
 
+def test_long_prompts_reach_the_tensor_core_recurrence(tmp_path):
+    """Prompts long enough for the state-space layers to run part by part on the tensor cores (bfloat16), whole, with a
+    decoded tail, and beside one another in one step with a short one: against the plain implementation, and against the
+    same prompts cut into portions that walk token by token."""
+    folder = cases.write_folder(str(tmp_path / "t"), cases.TENSOR, seed=5, dtype=torch.bfloat16)
+    cfg, w = cases.read_folder(folder)
+    requests = {"a": helpers.random_tokens(cfg["vocab"], 450, 31), "b": helpers.random_tokens(cfg["vocab"], 257, 32),
+                "c": helpers.random_tokens(cfg["vocab"], 5, 33)}
+    ref = {rid: _plain(cfg, w, toks) for rid, toks in requests.items()}
+    together = [{"entries": [{"id": rid, "tokens": toks, "want": list(range(len(toks)))} for rid, toks in requests.items()],
+                 "end": list(requests)}]
+    got = {}
+    for name, steps in (("whole", helpers.steps_whole(requests)), ("tail", helpers.steps_decode_tail(requests, tail=40)),
+                        ("together", together), ("portions", helpers.steps_portions(requests, sizes=(100, 64, 31, 2, 90)))):
+        pages = -(-helpers.max_live_tokens(requests, steps, rounding=16) // 16)
+        engine = build_engine(folder, EngineConfig(dtype="bfloat16", page_size=16, num_pages=pages, max_batch_size=4,
+                                                   max_seq_len=512, device=DEV))
+        got[name] = helpers.run_steps(engine, steps)
+        engine.cache.audit()
+        engine.close()
+        for rid in ref:
+            scale = float(ref[rid].abs().max())
+            rows = (got[name][rid] - ref[rid]).abs().amax(dim=-1) / scale
+            assert float((rows < 6e-2).float().mean()) >= 0.8 and float(rows.median()) < 3e-2, (name, rid)
+    for name in ("whole", "tail", "together"):
+        for rid in ref:
+            scale = float(ref[rid].abs().max())
+            rows = (got[name][rid] - got["portions"][rid]).abs().amax(dim=-1) / scale
+            assert float(rows.median()) < 2e-2, (name, rid)
+
+
 def test_long_decoding_through_captured_steps(tmp_path):
     """300 decoded tokens after a prompt of 40, three requests side by side: states, convolution tails, window edges and
     the pages given back behind them, step after step through replays of captured steps."""
