@@ -206,7 +206,8 @@ def test_state_space_decode_steps_against_their_twin(kernels, twin, dtype, H, P,
         state, tail = views[1].state, views[1].tail
 
 
-@pytest.mark.parametrize("H,P,N,G,taps", [(4, 64, 128, 2, 4), (2, 32, 64, 1, 3), (3, 16, 16, 3, 2), (2, 128, 32, 2, 4)])
+@pytest.mark.parametrize("H,P,N,G,taps", [(4, 64, 128, 2, 4), (2, 32, 64, 1, 3), (3, 16, 16, 3, 2), (2, 128, 32, 2, 4),
+                                          (1, 48, 80, 1, 4), (2, 80, 48, 2, 3), (2, 16, 256, 1, 4), (1, 256, 16, 1, 2)])
 @pytest.mark.parametrize("decay", [1.0, 40.0])
 def test_state_space_on_tensor_cores_keeps_float32_where_the_walk_does(kernels, H, P, N, G, taps, decay):
     """Long bfloat16 segments run as parts on the tensor cores, where every float32 factor enters as two bfloat16
