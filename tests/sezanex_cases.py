@@ -83,6 +83,15 @@ TENSOR = config(128, 260, [
 ], loop=(0, 3, 2))
 
 
+# keys and values of 128 (the other head size of the tensor-core attention), more query heads per key head, a window
+# longer than a key tile, a wide state with few heads, the looped range at the end
+WIDE = config(96, 180, [
+    layer(mamba2(1, 128, 16, 1, 1, 3), moe(5, 3, 48)),
+    layer(attention(4, 1, 128, 128, window=70, rot_dims=128, base=5000.0, scaling=(2.0, 64, 16.0, 2.0)), dense(96)),
+    layer(mamba2(4, 16, 48, 4, 2, 4), None),
+], loop=(1, 3, 2))
+
+
 def single(kind):
     """One layer with one mechanism and nothing beside it."""
     if kind == "attention":

@@ -284,7 +284,7 @@ def _plain(cfg, w, toks):
 
 
 @pytest.mark.parametrize("dtype,tol", [("float32", 1e-4), ("bfloat16", 6e-2)])
-@pytest.mark.parametrize("name", ["ALIGNED", "ODD", "PLAIN", "TENSOR"])
+@pytest.mark.parametrize("name", ["ALIGNED", "ODD", "PLAIN", "TENSOR", "WIDE"])
 def test_engine_matches_the_plain_implementation(tmp_path, dtype, tol, name):
     folder = cases.write_folder(str(tmp_path / name), getattr(cases, name), seed=3,
                                 dtype=torch.float32 if dtype == "float32" else torch.bfloat16)
