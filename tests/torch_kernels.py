@@ -130,6 +130,19 @@ class TorchKernels:
             return None
         return self._layernorm(residual, norm).to(out_dtype)
 
+    def add_layernorm_sum(self, residual, tensors, scales, row_term, norm, out_dtype):
+        for i, t in enumerate(tensors):
+            residual += t.to(torch.float32) * (1.0 if scales is None else scales[i])
+        if row_term is not None:
+            residual += row_term[0] * row_term[1]
+        if norm is None:
+            return None
+        return self._layernorm(residual, norm).to(out_dtype)
+
+    def add_row_vector(self, x, vector):
+        x.copy_((x.float() + vector).to(x.dtype))
+        return x
+
     # ------------------------------------------------------------------ latent attention
     @staticmethod
     def _rotate(x, positions, inv_freq, rotary_dim):
@@ -145,46 +158,59 @@ class TorchKernels:
         return out
 
     def latent_prepare(self, down, batch, q_rank, kv_rank, rot_dim, q_norm, kv_norm, eps, inv_freq, rotary_dim, view,
-                       write, out_dtype):
+                       write, out_dtype, amplitude=1.0):
         down = down.float()
-        cq = down[:, :q_rank]
-        cq = cq * torch.rsqrt(cq.pow(2).mean(-1, keepdim=True) + eps) * q_norm
+        cq = None
+        if q_rank:
+            cq = down[:, :q_rank]
+            cq = (cq * torch.rsqrt(cq.pow(2).mean(-1, keepdim=True) + eps) * q_norm).to(out_dtype)
+        if not (write and view is not None):
+            return cq
         c = down[:, q_rank:q_rank + kv_rank]
         c = c * torch.rsqrt(c.pow(2).mean(-1, keepdim=True) + eps) * kv_norm
         row = c
         if rot_dim:
-            shared = self._rotate(down[:, q_rank + kv_rank:q_rank + kv_rank + rot_dim], batch.positions, inv_freq, rotary_dim)
+            raw = down[:, q_rank + kv_rank:q_rank + kv_rank + rot_dim]
+            shared = self._rotate(raw, batch.positions, inv_freq, rotary_dim)
+            shared[:, :rotary_dim] *= amplitude
             row = torch.cat([c, shared], dim=-1)
-        if write and view is not None:
-            P = view.page_size
-            pos = batch.positions.long()
-            pages = view.block_table[batch.seg_of_token.long(), pos // P].long()
-            view.rows[pages, pos % P] = row.to(view.rows.dtype)
-        return cq.to(out_dtype)
+        P = view.page_size
+        pos = batch.positions.long()
+        pages = view.block_table[batch.seg_of_token.long(), pos // P].long()
+        view.rows[pages, pos % P] = row.to(view.rows.dtype)
+        return cq
 
     def heads_linear(self, x, w, out_dtype=None):
         """x [T, H, K] (any strides), w [H, N, K] -> [T, H, N]."""
         return torch.einsum("thk,hnk->thn", x.float(), w.float()).to(out_dtype or x.dtype)
 
-    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
+    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, amplitude=1.0, window="view"):
         T, H, R = q_latent.shape
         out = torch.empty(T, H, R, dtype=torch.float32, device=q_latent.device)
         P = view.page_size
         ql = q_latent.float()
-        qr = self._rotate(q_rot.float(), batch.positions, inv_freq, rotary_dim) if q_rot is not None else None
+        window = view.window if window == "view" else window
+        qr = None
+        if q_rot is not None:
+            qr = self._rotate(q_rot.float(), batch.positions, inv_freq, rotary_dim)
+            qr[..., :rotary_dim] *= amplitude
         start = 0
         for r, n in enumerate(batch.seg_lens):
             pos0 = batch.seg_pos0_list[r]
             ctx = pos0 + n
             n_pages = -(-ctx // P)
             rows = view.rows[view.block_table[r, :n_pages].long()].reshape(n_pages * P, -1)[:ctx].float()
+            rows = torch.where(torch.isfinite(rows), rows, torch.zeros_like(rows))     # pages behind the window may be anyone's by now
             scores = torch.einsum("thr,sr->hts", ql[start:start + n], rows[:, :R])
             if qr is not None:
                 scores = scores + torch.einsum("thd,sd->hts", qr[start:start + n], rows[:, R:])
             scores = scores * scale
             qpos = torch.arange(pos0, ctx, device=ql.device)[:, None]
             kpos = torch.arange(ctx, device=ql.device)[None, :]
-            scores = scores.masked_fill(~(kpos <= qpos)[None], float("-inf"))
+            visible = kpos <= qpos
+            if window:
+                visible = visible & (kpos > qpos - window)
+            scores = scores.masked_fill(~visible[None], float("-inf"))
             if sinks is not None:
                 full = torch.cat([scores, sinks.view(H, 1, 1).expand(H, n, 1)], dim=-1)
                 weights = torch.softmax(full, dim=-1)[..., :ctx]
@@ -194,8 +220,9 @@ class TorchKernels:
             start += n
         return out.to(q_latent.dtype)
 
-    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate):
-        mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim)
+    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate, amplitude=1.0,
+                             window="view"):
+        mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, amplitude, window)
         return self.gate_heads(self.heads_linear(mixed, w_uv), gate)
 
     def gate_heads(self, out, gate):
@@ -218,12 +245,21 @@ class TorchKernels:
     @staticmethod
     def _glu_clamped(gate_up, limit, alpha):
         inter = gate_up.shape[-1] // 2
+        if not limit > 0:                      # no clamps and no unit offset: the plain gated unit
+            g = gate_up[..., :inter].float()
+            return g * torch.sigmoid(alpha * g) * gate_up[..., inter:].float()
         g = gate_up[..., :inter].float().clamp(max=limit)
         u = gate_up[..., inter:].float().clamp(min=-limit, max=limit)
         return g * torch.sigmoid(alpha * g) * (u + 1.0)
 
     def linear_glu_clamped(self, x, w_gate_up, limit, alpha):
         return self._glu_clamped(self.linear(x, w_gate_up), limit, alpha).to(x.dtype)
+
+    def route_corrected(self, x, w_router, correction, experts, top, scale, floor):
+        s = torch.sigmoid(x.float() @ w_router.t())
+        order = torch.sort(s + correction, dim=-1, descending=True, stable=True).indices[:, :top]
+        chosen = torch.gather(s, 1, order)
+        return order.to(torch.int32), chosen / (chosen.sum(-1, keepdim=True) + floor) * scale
 
     def routed_experts(self, x, choice, weight, w_gate_up, w_down, limit, alpha, shared=None, shared_gate=None):
         T, top = choice.shape
@@ -235,7 +271,7 @@ class TorchKernels:
                 out[t] += weight[t, j] * self.linear(hidden, w_down[e]).float()[0]
         if shared is not None:
             shared_out = self.linear(self.linear_glu_clamped(x, shared[0], shared[2], alpha), shared[1])
-            out += shared_out.float() * shared_gate[:, None]
+            out += shared_out.float() * (shared_gate[:, None] if shared_gate is not None else 1.0)
         return out
 
     # ------------------------------------------------------------------ the float32 stream, several outputs at once
@@ -267,7 +303,7 @@ class TorchKernels:
     def glu_activation(self, gate_up, activation):
         inter = gate_up.shape[1] // 2
         g, u = gate_up[:, :inter].float(), gate_up[:, inter:].float()
-        act = g * torch.sigmoid(g) if activation == "silu" else self._gelu_tanh(g)
+        act = g * torch.sigmoid(g) if activation == "silu" else (torch.relu(g) if activation == "relu" else self._gelu_tanh(g))
         return (act * u).to(gate_up.dtype)
 
     def activation(self, x, activation, out_dtype):
@@ -415,11 +451,107 @@ class TorchKernels:
         gates = self.heads_linear(u.view(-1, B, C // B), w_gates, out_dtype=torch.float32)
         return self.gated_recurrence(u, gates, gate_bias, rate, yx, bias_yx, batch, view, write_state)
 
+    # ------------------------------------------------------------------ token shift, low-rank maps, matrix states
+    def token_shift(self, x, mu, batch, view):
+        T, width = x.shape
+        out = torch.empty(T, mu.shape[0], width, dtype=torch.float32, device=x.device)
+        xf = x.float()
+        start = 0
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            before = torch.cat([view.tail[slot][:1].float(), xf[start:start + n - 1]], 0)
+            cur = xf[start:start + n]
+            out[start:start + n] = cur[:, None, :] + (before - cur)[:, None, :] * mu[None]
+            start += n
+        return out.to(x.dtype)
+
+    def lowrank_expand(self, x, w, bias, in_act, out_kind, rate=None):
+        z = x.float()
+        if in_act == "tanh":
+            z = torch.tanh(z)
+        z = z @ w.float().t()
+        if bias is not None:
+            z = z + bias
+        if out_kind == "neg_exp":
+            return -torch.exp(z)
+        if out_kind == "neg_rate_softplus":
+            heads = rate.shape[0]
+            sp = torch.nn.functional.softplus(z, threshold=30.0)
+            return -(sp.view(z.shape[0], heads, -1) * rate[None, :, None]).reshape(z.shape)
+        assert out_kind == "none"
+        return z
+
+    def shifted_state(self, rkvg, log_decay, bonus, norm_w, eps, heads, dim, x, batch, view, write_state=True):
+        T = rkvg.shape[0]
+        r, k, v = (rkvg[:, i].float().view(T, heads, dim) for i in range(3))
+        g = rkvg[:, 3].float()
+        w = torch.exp(log_decay).view(T, heads, dim)
+        out = torch.empty(T, heads, dim, dtype=torch.float32, device=x.device)
+        start = 0
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            S = view.state[slot].clone()
+            for t in range(start, start + n):
+                kv = k[t][:, :, None] * v[t][:, None, :]
+                out[t] = torch.einsum("hkv,hk->hv", S + bonus[:, :, None] * kv, r[t])
+                S = w[t][:, :, None] * S + kv
+            if write_state:
+                view.state[slot] = S
+                view.tail[slot][0] = x[start + n - 1]
+            start += n
+        out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + eps)
+        return (out.reshape(T, heads * dim) * norm_w * (g * torch.sigmoid(g))).to(x.dtype)
+
+    def short_conv_silu(self, x, conv_w, batch, view):
+        T, C = x.shape
+        taps = conv_w.shape[1]
+        out = torch.empty(T, C, dtype=torch.float32, device=x.device)
+        start = 0
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            kept = view.tail[slot][:taps - 1].float() if taps > 1 else x[:0].float()
+            seq = torch.cat([kept, x[start:start + n].float()], 0)
+            acc = torch.zeros(n, C, dtype=torch.float32, device=x.device)
+            for j in range(taps):
+                acc = acc + seq[j:j + n] * conv_w[:, j]
+            out[start:start + n] = acc * torch.sigmoid(acc)
+            start += n
+        return out.to(x.dtype)
+
+    def delta_rule(self, u, raw, beta, log_decay, gate, norm_w, eps, heads, kv_heads, dim, vdim, batch, view, write_state=True):
+        T = u.shape[0]
+        qk = kv_heads * dim
+        uf = u.float()
+        q, k = uf[:, :qk].view(T, kv_heads, dim), uf[:, qk:2 * qk].view(T, kv_heads, dim)
+        v = uf[:, 2 * qk:].view(T, heads, vdim)
+        q = q / torch.sqrt(q.pow(2).sum(-1, keepdim=True) + 1e-6) * dim ** -0.5
+        k = k / torch.sqrt(k.pow(2).sum(-1, keepdim=True) + 1e-6)
+        rep = heads // kv_heads
+        q, k = q.repeat_interleave(rep, dim=1), k.repeat_interleave(rep, dim=1)
+        b = torch.sigmoid(beta.float())
+        g = torch.exp(log_decay).view(T, heads, dim)
+        out = torch.empty(T, heads, vdim, dtype=torch.float32, device=u.device)
+        keep = view.taps - 1
+        start = 0
+        for n, slot in zip(batch.seg_lens, batch.seg_slot_list):
+            S = view.state[slot].clone()
+            for t in range(start, start + n):
+                S = g[t][:, :, None] * S
+                d = b[t][:, None] * (v[t] - torch.einsum("hkv,hk->hv", S, k[t]))
+                S = S + k[t][:, :, None] * d[:, None, :]
+                out[t] = torch.einsum("hkv,hk->hv", S, q[t])
+            if write_state:
+                view.state[slot] = S
+                if keep > 0:
+                    view.tail[slot][:keep] = torch.cat([view.tail[slot][:keep], raw[start:start + n].to(view.tail.dtype)], 0)[-keep:]
+            start += n
+        out = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + eps) * norm_w
+        return (out.reshape(T, heads * vdim) * torch.sigmoid(gate.float())).to(u.dtype)
+
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
-                           write_kv=True, whole=False, amplitude=1.0):
+                           write_kv=True, whole=False, amplitude=1.0, bias=None, q_temp=None):
         T = qkv.shape[0]
         n_qk = heads + kv_heads
+        if bias is not None:
+            qkv.copy_((qkv.float() + bias).to(qkv.dtype))
         x = qkv[:, :n_qk * dim].float().clone().view(T, n_qk, dim)
         if q_norm is not None and whole:
             q, k = x[:, :heads].reshape(T, -1), x[:, heads:].reshape(T, -1)
@@ -429,6 +561,9 @@ class TorchKernels:
         elif q_norm is not None:
             x = x / torch.sqrt(x.pow(2).mean(-1, keepdim=True) + eps)
             x = torch.cat([x[:, :heads] * q_norm, x[:, heads:] * k_norm], 1)
+        if q_temp is not None:
+            runs = torch.div(batch.positions + 1, q_temp[1], rounding_mode="floor").to(torch.float32)
+            x[:, :heads] = x[:, :heads] * (1.0 + q_temp[0] * torch.log(runs + 1.0))[:, None, None]
         if rotary_dim:
             half = rotary_dim // 2
             angles = batch.positions.to(torch.float32)[:, None] * inv_freq[None, :]
@@ -444,7 +579,7 @@ class TorchKernels:
         view.keys[pages, :, pos % P, :] = qkv[:, heads * dim:n_qk * dim].view(T, kv_heads, dim)
         view.values[pages, :, pos % P, :] = qkv[:, n_qk * dim:].view(T, kv_heads, vdim)
 
-    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view):
+    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view, distance_bias=None):
         T = qkv.shape[0]
         q_all = qkv[:, :heads * dim].float().view(T, heads, dim)
         out = torch.empty(T, heads, vdim, dtype=torch.float32, device=qkv.device)
@@ -464,6 +599,9 @@ class TorchKernels:
                 scores = softcap * torch.tanh(scores / softcap)
             qpos = torch.arange(pos0, ctx, device=qkv.device)[:, None]
             kpos = torch.arange(ctx, device=qkv.device)[None, :]
+            if distance_bias is not None:
+                far = distance_bias.shape[1] - 1
+                scores = scores + distance_bias[:, (qpos - kpos).clamp(0, far)]
             visible = kpos <= qpos
             if view.window:
                 visible &= kpos > qpos - view.window

@@ -20,12 +20,15 @@ import torch
 @dataclass(frozen=True)
 class TensorSpec:
     """One checkpoint tensor: its full name, its shape, and whether it holds
-    floating-point values ("float") or an integer table ("int")."""
+    floating-point values ("float") or an integer table ("int"). A size of None is read from
+    the checkpoint (the rank of a low-rank map that no configuration key gives); `free_size`
+    stands in for it where tensors are made up (random weights)."""
 
     name: str
     shape: Tuple[int, ...]
     kind: str = "float"
     optional: bool = False
+    free_size: int = 16
 
 
 # ----------------------------------------------------------------------------- what a mixer asks of the cache
@@ -278,13 +281,41 @@ class PendingDelta:
 
 class SumDelta(PendingDelta):
     """Several sub-layer outputs (any dtype, each [rows, width]) that join the stream together: a norm that knows
-    the kind adds them in its own kernel, everything else calls settle()."""
+    the kind adds them in its own kernel, everything else calls settle(). `scales`: a factor for each tensor (None:
+    all one); `row_term`: (float32 vector [width], factor), the same for every row (a bias on its way into the stream)."""
 
-    def __init__(self, tensors, kernels):
-        self.tensors, self.kernels = [t for t in tensors if t is not None], kernels
+    def __init__(self, tensors, kernels, scales=None, row_term=None):
+        keep = [i for i, t in enumerate(tensors) if t is not None]
+        self.tensors, self.kernels = [tensors[i] for i in keep], kernels
+        self.scales = None if scales is None else [float(scales[i]) for i in keep]
+        self.row_term = row_term
+        if self.scales is not None and all(s == 1.0 for s in self.scales):
+            self.scales = None
+
+    @property
+    def plain(self) -> bool:
+        return self.scales is None and self.row_term is None
 
     def settle(self, residual) -> None:
-        self.kernels.stream_add_norm(residual, self.tensors)
+        if self.plain:
+            self.kernels.stream_add_norm(residual, self.tensors)
+        else:
+            self.kernels.add_layernorm_sum(residual, self.tensors, self.scales, self.row_term, None, None)
+
+
+class ScaledParts:
+    """What a mixer made of mixers returns when its result is a weighted sum that the block may as well form on the
+    way into the stream: terms [(tensor [rows, width], factor)] and an optional row term (vector, factor).
+    materialize() forms the sum as a float32 tensor for a caller that wants one."""
+
+    def __init__(self, terms, row_term, kernels):
+        self.terms, self.row_term, self.kernels = terms, row_term, kernels
+
+    def materialize(self):
+        first = self.terms[0][0]
+        out = torch.zeros(first.shape, dtype=torch.float32, device=first.device)
+        self.kernels.add_layernorm_sum(out, [t for t, _ in self.terms], [s for _, s in self.terms], self.row_term, None, None)
+        return out
 
 
 class _Added:

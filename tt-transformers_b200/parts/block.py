@@ -15,7 +15,7 @@ tensors only, as before.
 
 from __future__ import annotations
 
-from .base import ADDED, Block, DeferredNorm, PendingDelta, SumDelta, register_part
+from .base import ADDED, Block, DeferredNorm, PendingDelta, ScaledParts, SumDelta, register_part
 
 
 def _normed(norm, consumer, x, delta):
@@ -118,15 +118,17 @@ register_part("block", "sandwich_mixer_only", SandwichMixerBlock)
 
 
 class ParallelBlock(Block):
-    """One norm, and both sub-layers read its output: h = norm1(x); x += mixer(h) + ff(h). The two outputs travel
+    """One norm, and both sub-layers read its output: h = norm1(x); x += m (mixer(h) + ff(h)). The outputs travel
     on as one SumDelta and are added to the float32 stream inside the next norm's kernel (the norm part must take a
-    SumDelta: kind `rmsnorm`)."""
+    SumDelta: kinds `rmsnorm` and `layernorm`). `residual_mult` is m. A mixer that returns a weighted sum of parts
+    (ScaledParts) has its parts added there one by one, each with its factor times m."""
 
     slots = {"norm1": "norm", "mixer": "mixer", "feed_forward": "feed_forward"}
     takes_pending = True
 
-    def __init__(self, norm1, mixer, feed_forward=None):
+    def __init__(self, norm1, mixer, feed_forward=None, residual_mult: float = 1.0):
         self.norm1, self.mixer, self.feed_forward = norm1, mixer, feed_forward
+        self.residual_mult = float(residual_mult)
 
     def forward(self, x, delta, batch, cache, write_cache=True):
         if isinstance(delta, PendingDelta) and not isinstance(delta, SumDelta):
@@ -137,7 +139,12 @@ class ParallelBlock(Block):
         h = self.norm1.forward_add(x, delta)
         mixed = self.mixer.forward(h, batch, cache, write_cache)
         fed = self.feed_forward.forward(h, batch) if self.feed_forward is not None else None
-        return x, SumDelta([mixed, fed], self.mixer.runtime.kernels)
+        m = self.residual_mult
+        if not isinstance(mixed, ScaledParts):
+            return x, SumDelta([mixed, fed], self.mixer.runtime.kernels, scales=None if m == 1.0 else [m, m])
+        terms = list(mixed.terms) + ([(fed, 1.0)] if fed is not None else [])
+        row = None if mixed.row_term is None else (mixed.row_term[0], mixed.row_term[1] * m)
+        return x, SumDelta([t for t, _ in terms], self.mixer.runtime.kernels, scales=[s * m for _, s in terms], row_term=row)
 
 
 class ParallelMixerBlock(ParallelBlock):

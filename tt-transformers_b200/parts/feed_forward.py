@@ -46,7 +46,7 @@ register_part("feed_forward", "swiglu", SwiGLU)
 
 class GatedMLP(FeedForward):
     """W_down (act(W_gate h) * (W_up h)) with the activation and the tensor names as parameters: `activation`
-    "silu" or "gelu_tanh" (0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3)))); `names` = (gate, up, down) after
+    "silu", "relu" or "gelu_tanh" (0.5 z (1 + tanh(sqrt(2/pi) (z + 0.044715 z^3)))); `names` = (gate, up, down) after
     `prefix`. The activation is computed in float32 on the product's output."""
 
     graph_safe = True
@@ -54,8 +54,8 @@ class GatedMLP(FeedForward):
     def __init__(self, width: int, inter: int, prefix: str, activation: str = "silu", names=("gate", "up", "down")):
         self.width, self.inter, self.prefix, self.activation = int(width), int(inter), prefix, activation
         self.names = tuple(names)
-        if activation not in ("silu", "gelu_tanh"):
-            raise ValueError(f"activation {activation!r} is not known; known: ['silu', 'gelu_tanh']")
+        if activation not in ("silu", "gelu_tanh", "relu"):
+            raise ValueError(f"activation {activation!r} is not known; known: ['silu', 'gelu_tanh', 'relu']")
 
     def tensor_specs(self):
         p, (g, u, d) = self.prefix, self.names

@@ -47,6 +47,9 @@ class RMSNorm(Norm):
             delta = None                         # prepared for another norm: the stream itself is up to date
         if delta is ADDED:
             delta = None
+        if isinstance(delta, SumDelta) and not delta.plain:
+            delta.settle(residual)               # factors and a row term: added first, by the kernel that knows them
+            delta = None
         if isinstance(delta, SumDelta) or self.unit_offset or (delta is not None and delta.dtype != self.runtime.dtype):
             # several outputs at once, outputs in another dtype than the compute dtype, or the 1 + w form
             deltas = delta.tensors if isinstance(delta, SumDelta) else ([delta] if delta is not None else [])
@@ -81,9 +84,15 @@ class LayerNorm(Norm):
             self.bias = tensors[self.bias_name].to(device=runtime.device, dtype=torch.float32).contiguous()
 
     def forward_add(self, residual, delta, after: "LayerNorm" = None, mult: float = 1.0):
-        """residual += mult * (after(delta) if `after` else delta), then this norm of the residual."""
+        """residual += mult * (after(delta) if `after` else delta), then this norm of the residual. A SumDelta (several
+        outputs with a factor each, and a row term) is added in the same kernel."""
         if delta is ADDED or isinstance(delta, DeferredNorm):
             delta = None
+        if isinstance(delta, SumDelta):
+            if after is not None:
+                raise ValueError("a sum of sub-layer outputs joins the stream as it is, without a norm of its own")
+            return self.runtime.kernels.add_layernorm_sum(residual, delta.tensors, delta.scales, delta.row_term, self,
+                                                          self.runtime.dtype)
         return self.runtime.kernels.add_layernorm(residual, delta, after, mult, self, self.runtime.dtype)
 
     def join(self, residual, delta, mult: float = 1.0):

@@ -30,6 +30,7 @@ _ARCHITECTURES: Dict[str, Union[str, Architecture]] = {
     "Bozavik": "tt_transformers_b200.models.bozavik",
     "Pedazen": "tt_transformers_b200.models.pedazen",
     "Sezanex": "tt_transformers_b200.models.sezanex",
+    "Bufolorn": "tt_transformers_b200.models.bufolorn",
 }
 
 

@@ -87,7 +87,7 @@ def check_tensors(tensors: Dict[str, torch.Tensor], specs: List[TensorSpec],
                 missing.append(f"{spec.name} {list(spec.shape)}")
             continue
         t = tensors[spec.name]
-        if tuple(t.shape) != tuple(spec.shape):
+        if len(t.shape) != len(spec.shape) or any(want is not None and have != want for have, want in zip(t.shape, spec.shape)):
             wrong.append(f"{spec.name}: shape {list(t.shape)}, expected {list(spec.shape)}")
         elif spec.kind == "float" and not t.dtype.is_floating_point:
             wrong.append(f"{spec.name}: holds {t.dtype}, expected floating-point values")

@@ -33,12 +33,13 @@ def random_tensors(config_dict: dict, seed: int, std: float = 0.02, norm_std: fl
     for spec in model.tensor_specs():
         if spec.kind == "int":
             raise ValueError(f"{spec.name}: random integer tables are not defined")
-        if len(spec.shape) == 1:
-            t = torch.ones(spec.shape, dtype=torch.float32, device=device)
+        shape = tuple(spec.free_size if n is None else n for n in spec.shape)
+        if len(shape) == 1:
+            t = torch.ones(shape, dtype=torch.float32, device=device)
             if norm_std:
-                t = t + torch.randn(spec.shape, generator=gen, dtype=torch.float32, device=device) * norm_std
+                t = t + torch.randn(shape, generator=gen, dtype=torch.float32, device=device) * norm_std
         else:
-            t = torch.randn(spec.shape, generator=gen, dtype=torch.float32, device=device) * std
+            t = torch.randn(shape, generator=gen, dtype=torch.float32, device=device) * std
         out[spec.name] = t.to(dtype).contiguous()
     return out
 
