@@ -12,7 +12,8 @@
 //
 // Options, all off by default: values of another size than keys (value_dim); a cap on the scores,
 // score = cap * tanh(score / cap); chunks (lo = the first position of the chunk of `chunk` positions that
-// holds p); a sink per head, one more term exp(sink_h) of the softmax's denominator without a value.
+// holds p); a sink per head, one more term exp(sink_h) of the softmax's denominator without a value; a bias by
+// distance, dist_bias[h, min(p - key, far)] (float32 [heads, far + 1]), added to the capped score.
 #include "common.cuh"
 
 #define ATT_TILE 128
@@ -27,7 +28,7 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
                                const int* __restrict__ block_table, int table_width, int page_size,
                                int heads, int kv_heads, int head_dim, float scale, int window, int num_pages,
                                int* __restrict__ status, int value_dim, float softcap, int chunk,
-                               const float* __restrict__ sinks) {
+                               const float* __restrict__ sinks, const float* __restrict__ dist_bias, int far) {
     extern __shared__ float smem[];
     float* q = smem;                                   // [head_dim, padded to an even count]
     float* prob = smem + ((head_dim + 1) & ~1);        // [ATT_TILE]
@@ -80,6 +81,7 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
             }
             score = dot * scale;
             if (softcap > 0.f) score = softcap * tanhf(score / softcap);
+            if (dist_bias != nullptr) score += dist_bias[(size_t)h * (far + 1) + min(pos - key, far)];   // not scaled, not capped
         }
         const float tile_max = block_max(score, scratch);
         const float new_max = fmaxf(run_max, tile_max);       // finite: every tile holds at least one visible key
@@ -118,17 +120,17 @@ paged_attention_generic_kernel(const T* __restrict__ qkv, int q_row_stride, T* _
     }
 }
 
-TTB_EXPORT int ttb_paged_attention_generic_ext(const void* qkv, int q_row_stride, void* out, int dtype,
+TTB_EXPORT int ttb_paged_attention_generic_bias(const void* qkv, int q_row_stride, void* out, int dtype,
                                            const int* positions, const int* seg_of_token, const void* key_pages,
                                            const void* value_pages, const int* block_table, int table_width,
                                            int page_size, int tokens, int heads, int kv_heads, int head_dim,
                                            float scale, int window, int num_pages, int* status, int value_dim, float softcap,
-                                           int chunk, const float* sinks, cudaStream_t stream) {
+                                           int chunk, const float* sinks, const float* dist_bias, int far, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!qkv || !out || !positions || !seg_of_token || !key_pages || !value_pages || !block_table || !status)
         return TTB_ERR_ARGUMENT;
     if (head_dim < 1 || value_dim < 1 || value_dim > ATT_MAX_ACC * ATT_THREADS || head_dim > 4096) return TTB_ERR_UNSUPPORTED;
-    if (softcap < 0.f || chunk < 0) return TTB_ERR_ARGUMENT;
+    if (softcap < 0.f || chunk < 0 || (dist_bias && far < 0)) return TTB_ERR_ARGUMENT;
     if (kv_heads < 1 || heads % kv_heads != 0) return TTB_ERR_UNSUPPORTED;
     if (heads > 65535) return TTB_ERR_UNSUPPORTED;
     const size_t smem = (size_t)(((head_dim + 1) & ~1) + ATT_TILE) * sizeof(float) + ATT_TILE * sizeof(size_t);
@@ -138,16 +140,27 @@ TTB_EXPORT int ttb_paged_attention_generic_ext(const void* qkv, int q_row_stride
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, positions, seg_of_token,
             (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
-            heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks);
+            heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks, dist_bias, far);
     } else if (dtype == TTB_DTYPE_F32) {
         if ((head_dim & 7) == 0 && (!aligned16(key_pages))) return TTB_ERR_ARGUMENT;
         paged_attention_generic_kernel<<<grid, ATT_THREADS, smem, stream>>>(
             (const float*)qkv, q_row_stride, (float*)out, positions, seg_of_token, (const float*)key_pages,
-            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks);
+            (const float*)value_pages, block_table, table_width, page_size, heads, kv_heads, head_dim, scale, window, num_pages, status, value_dim, softcap, chunk, sinks, dist_bias, far);
     } else {
         return TTB_ERR_UNSUPPORTED;
     }
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_paged_attention_generic_ext(const void* qkv, int q_row_stride, void* out, int dtype,
+                                           const int* positions, const int* seg_of_token, const void* key_pages,
+                                           const void* value_pages, const int* block_table, int table_width,
+                                           int page_size, int tokens, int heads, int kv_heads, int head_dim,
+                                           float scale, int window, int num_pages, int* status, int value_dim, float softcap,
+                                           int chunk, const float* sinks, cudaStream_t stream) {
+    return ttb_paged_attention_generic_bias(qkv, q_row_stride, out, dtype, positions, seg_of_token, key_pages, value_pages, block_table,
+                                            table_width, page_size, tokens, heads, kv_heads, head_dim, scale, window, num_pages, status,
+                                            value_dim, softcap, chunk, sinks, nullptr, 0, stream);
 }
 
 TTB_EXPORT int ttb_paged_attention_generic(const void* qkv, int q_row_stride, void* out, int dtype,

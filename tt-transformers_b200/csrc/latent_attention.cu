@@ -27,7 +27,7 @@ latent_prepare_kernel(const float* __restrict__ down, int ld_down, int q_rank, i
                       const float* __restrict__ inv_freq, int rotary_dim, const int* __restrict__ positions,
                       const int* __restrict__ seg_of_token, TO* __restrict__ cq, TO* __restrict__ rows,
                       const int* __restrict__ block_table, int table_width, int page_size, int num_pages, int write,
-                      int tokens, int* __restrict__ status) {
+                      int tokens, int* __restrict__ status, float amplitude) {
     pdl_wait();
     pdl_launch_dependents();
     const int lane = threadIdx.x & 31;
@@ -64,6 +64,8 @@ latent_prepare_kernel(const float* __restrict__ down, int ld_down, int q_rank, i
     for (int i = lane; i < half; i += 32) {
         float sn, cs;
         sincosf((float)pos * inv_freq[i], &sn, &cs);
+        sn *= amplitude;
+        cs *= amplitude;
         const float u = r_src[i], v = r_src[i + half];
         dst[kv_rank + i] = from_float<TO>(u * cs - v * sn);
         dst[kv_rank + i + half] = from_float<TO>(v * cs + u * sn);
@@ -71,28 +73,40 @@ latent_prepare_kernel(const float* __restrict__ down, int ld_down, int q_rank, i
     for (int i = rotary_dim + lane; i < rot_dim; i += 32) dst[kv_rank + i] = from_float<TO>(r_src[i]);
 }
 
-TTB_EXPORT int ttb_latent_prepare(const float* down, int ld_down, int q_rank, int kv_rank, int rot_dim,
+// q_rank 0: no query latent (q_norm and cq may be null); amplitude: what the rotation's cosines and sines are multiplied by.
+TTB_EXPORT int ttb_latent_prepare_ext(const float* down, int ld_down, int q_rank, int kv_rank, int rot_dim,
                                   const float* q_norm, const float* kv_norm, float eps, const float* inv_freq,
                                   int rotary_dim, const int* positions, const int* seg_of_token, void* cq, void* rows,
                                   int dtype, const int* block_table, int table_width, int page_size, int num_pages,
-                                  int write, int tokens, int* status, cudaStream_t stream) {
+                                  int write, int tokens, int* status, float amplitude, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
-    if (!down || !q_norm || !kv_norm || !cq || !positions || !seg_of_token || !status) return TTB_ERR_ARGUMENT;
-    if (write && (!rows || !block_table)) return TTB_ERR_ARGUMENT;
+    if (!down || !positions || !seg_of_token || !status || q_rank < 0) return TTB_ERR_ARGUMENT;
+    if (q_rank > 0 && (!q_norm || !cq)) return TTB_ERR_ARGUMENT;
+    if (write && (!rows || !block_table || !kv_norm)) return TTB_ERR_ARGUMENT;
     if (rot_dim < 0 || rotary_dim < 0 || rotary_dim > rot_dim || (rotary_dim & 1) || (rotary_dim > 0 && !inv_freq))
         return TTB_ERR_ARGUMENT;
     const int blocks = (tokens + LP_WARPS - 1) / LP_WARPS;
     if (dtype == TTB_DTYPE_BF16)
         ttb_launch(latent_prepare_kernel<__nv_bfloat16>, blocks, LP_WARPS * 32, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim,
                    q_norm, kv_norm, eps, inv_freq, rotary_dim, positions, seg_of_token, (__nv_bfloat16*)cq,
-                   (__nv_bfloat16*)rows, block_table, table_width, page_size, num_pages, write, tokens, status);
+                   (__nv_bfloat16*)rows, block_table, table_width, page_size, num_pages, write, tokens, status, amplitude);
     else if (dtype == TTB_DTYPE_F32)
         ttb_launch(latent_prepare_kernel<float>, blocks, LP_WARPS * 32, 0, stream, down, ld_down, q_rank, kv_rank, rot_dim, q_norm,
                    kv_norm, eps, inv_freq, rotary_dim, positions, seg_of_token, (float*)cq, (float*)rows, block_table,
-                   table_width, page_size, num_pages, write, tokens, status);
+                   table_width, page_size, num_pages, write, tokens, status, amplitude);
     else
         return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_latent_prepare(const float* down, int ld_down, int q_rank, int kv_rank, int rot_dim,
+                                  const float* q_norm, const float* kv_norm, float eps, const float* inv_freq,
+                                  int rotary_dim, const int* positions, const int* seg_of_token, void* cq, void* rows,
+                                  int dtype, const int* block_table, int table_width, int page_size, int num_pages,
+                                  int write, int tokens, int* status, cudaStream_t stream) {
+    return ttb_latent_prepare_ext(down, ld_down, q_rank, kv_rank, rot_dim, q_norm, kv_norm, eps, inv_freq, rotary_dim, positions,
+                                  seg_of_token, cq, rows, dtype, block_table, table_width, page_size, num_pages, write, tokens,
+                                  status, 1.f, stream);
 }
 
 // ---------------------------------------------------------------- latent_attention_generic
@@ -105,7 +119,7 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
                                 const int* __restrict__ block_table, int table_width, int page_size, int heads,
                                 int latent, int extra, float scale, const float* __restrict__ sinks,
                                 const float* __restrict__ inv_freq, int rotary_dim, int window, int num_pages,
-                                int* __restrict__ status) {
+                                int* __restrict__ status, float amplitude) {
     extern __shared__ __align__(16) float smem[];
     const int dk = latent + extra, dk_pad = (dk + 3) & ~3;
     float* q = smem;                                       // [LA_HEADS, dk_pad]
@@ -137,7 +151,7 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
                 float sn, cs;
                 sincosf((float)pos * inv_freq[f], &sn, &cs);
                 const float other = to_float(src[d < half ? d + half : d - half]);
-                v = d < half ? v * cs - other * sn : v * cs + other * sn;
+                v = (d < half ? v * cs - other * sn : v * cs + other * sn) * amplitude;
             }
             q[h * dk_pad + latent + d] = v;
         }
@@ -244,13 +258,13 @@ latent_attention_generic_kernel(const T* __restrict__ q_lat, long long ql_stride
     }
 }
 
-TTB_EXPORT int ttb_latent_attention_generic(const void* q_lat, long long ql_stride_t, long long ql_stride_h,
+TTB_EXPORT int ttb_latent_attention_generic_ext(const void* q_lat, long long ql_stride_t, long long ql_stride_h,
                                             const void* q_rot, long long qr_stride_t, long long qr_stride_h, void* out,
                                             int dtype, const int* positions, const int* seg_of_token, const void* rows,
                                             const int* block_table, int table_width, int page_size, int tokens,
                                             int heads, int latent, int extra, float scale, const float* sinks,
                                             const float* inv_freq, int rotary_dim, int window, int num_pages,
-                                            int* status, cudaStream_t stream) {
+                                            int* status, float amplitude, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!q_lat || !out || !positions || !seg_of_token || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
     if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
@@ -270,13 +284,25 @@ TTB_EXPORT int ttb_latent_attention_generic(const void* q_lat, long long ql_stri
         ttb_launch(latent_attention_generic_kernel<T>, grid, LA_THREADS, smem, stream, (const T*)q_lat, ql_stride_t,  \
                    ql_stride_h, (const T*)q_rot, qr_stride_t, qr_stride_h, (T*)out, positions, seg_of_token,         \
                    (const T*)rows, block_table, table_width, page_size, heads, latent, extra, scale, sinks, inv_freq, \
-                   rotary_dim, window, num_pages, status);                                                           \
+                   rotary_dim, window, num_pages, status, amplitude);                                                \
     } while (0)
     if (dtype == TTB_DTYPE_BF16) LA_LAUNCH(__nv_bfloat16);
     else if (dtype == TTB_DTYPE_F32) LA_LAUNCH(float);
     else return TTB_ERR_UNSUPPORTED;
 #undef LA_LAUNCH
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_latent_attention_generic(const void* q_lat, long long ql_stride_t, long long ql_stride_h,
+                                            const void* q_rot, long long qr_stride_t, long long qr_stride_h, void* out,
+                                            int dtype, const int* positions, const int* seg_of_token, const void* rows,
+                                            const int* block_table, int table_width, int page_size, int tokens,
+                                            int heads, int latent, int extra, float scale, const float* sinks,
+                                            const float* inv_freq, int rotary_dim, int window, int num_pages,
+                                            int* status, cudaStream_t stream) {
+    return ttb_latent_attention_generic_ext(q_lat, ql_stride_t, ql_stride_h, q_rot, qr_stride_t, qr_stride_h, out, dtype, positions,
+                                            seg_of_token, rows, block_table, table_width, page_size, tokens, heads, latent, extra,
+                                            scale, sinks, inv_freq, rotary_dim, window, num_pages, status, 1.f, stream);
 }
 
 // ---------------------------------------------------------------- gate_heads

@@ -169,3 +169,72 @@ TTB_EXPORT int ttb_add_layernorm(float* residual, const void* delta, int delta_d
 #undef LN_LAUNCH
     return ttb_launch_status();
 }
+
+// Several sub-layer outputs at once, each with a factor, and a vector that is the same for every row:
+//   residual += sum_i scale_i * term_i + row_scale * row_vector;   out = norm(residual)  (norm absent: nothing is written)
+// Terms are float32 or bfloat16 [rows, width], contiguous. One block per row, the row in shared memory between the passes.
+#define LN_MAX_TERMS 4
+struct LnTerms {
+    const void* ptr[LN_MAX_TERMS];
+    int dtype[LN_MAX_TERMS];
+    float scale[LN_MAX_TERMS];
+    int count;
+};
+
+template <typename TO>
+__global__ void __launch_bounds__(LN_THREADS)
+add_layernorm_sum_kernel(float* __restrict__ residual, const LnTerms terms, const float* __restrict__ row_vector, float row_scale,
+                         const float* __restrict__ norm_w, const float* __restrict__ norm_b, float norm_eps,
+                         TO* __restrict__ out, int width) {
+    extern __shared__ float row[];
+    __shared__ float scratch[32];
+    pdl_wait();
+    pdl_launch_dependents();
+    float* res = residual + (size_t)blockIdx.x * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        float v = res[c];
+        for (int i = 0; i < terms.count; ++i) {
+            const size_t at = (size_t)blockIdx.x * width + c;
+            const float d = terms.dtype[i] == TTB_DTYPE_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(terms.ptr[i])[at])
+                                                             : reinterpret_cast<const float*>(terms.ptr[i])[at];
+            v = fmaf(terms.scale[i], d, v);
+        }
+        if (row_vector != nullptr) v = fmaf(row_scale, row_vector[c], v);
+        if (terms.count > 0 || row_vector != nullptr) res[c] = v;
+        row[c] = v;
+    }
+    if (norm_w == nullptr) return;
+    __syncthreads();
+    float mean, rstd;
+    ln_stats(row, width, norm_eps, scratch, mean, rstd);
+    TO* o = out + (size_t)blockIdx.x * width;
+    for (int c = threadIdx.x; c < width; c += blockDim.x)
+        o[c] = from_float<TO>((row[c] - mean) * rstd * norm_w[c] + (norm_b != nullptr ? norm_b[c] : 0.f));
+}
+
+TTB_EXPORT int ttb_add_layernorm_sum(float* residual, const void* const* term_ptrs, const int* term_dtypes, const float* term_scales,
+                                     int count, const float* row_vector, float row_scale, const float* norm_w, const float* norm_b,
+                                     float norm_eps, void* out, int out_dtype, int rows, int width, cudaStream_t stream) {
+    if (rows == 0) return TTB_OK;
+    if (!residual || width < 1 || count < 0 || count > LN_MAX_TERMS || (norm_w && !out)) return TTB_ERR_ARGUMENT;
+    LnTerms terms = {};
+    terms.count = count;
+    for (int i = 0; i < count; ++i) {
+        if (!term_ptrs[i] || (term_dtypes[i] != TTB_DTYPE_BF16 && term_dtypes[i] != TTB_DTYPE_F32)) return TTB_ERR_ARGUMENT;
+        terms.ptr[i] = term_ptrs[i]; terms.dtype[i] = term_dtypes[i]; terms.scale[i] = term_scales[i];
+    }
+    const size_t smem = (size_t)width * sizeof(float);
+    if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    if (out_dtype == TTB_DTYPE_BF16 || !norm_w) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(add_layernorm_sum_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ttb_launch(add_layernorm_sum_kernel<__nv_bfloat16>, rows, LN_THREADS, smem, stream, residual, terms, row_vector, row_scale,
+                   norm_w, norm_b, norm_eps, (__nv_bfloat16*)out, width);
+    } else if (out_dtype == TTB_DTYPE_F32) {
+        if (smem > 48 * 1024) cudaFuncSetAttribute(add_layernorm_sum_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        ttb_launch(add_layernorm_sum_kernel<float>, rows, LN_THREADS, smem, stream, residual, terms, row_vector, row_scale, norm_w,
+                   norm_b, norm_eps, (float*)out, width);
+    } else {
+        return TTB_ERR_UNSUPPORTED;
+    }
+    return ttb_launch_status();
+}

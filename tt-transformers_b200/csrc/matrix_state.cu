@@ -1,0 +1,412 @@
+// Mixers with a float32 matrix state per head and request, walked token by token:
+//
+//   shifted_state:  o_t = (S + diag(u) k_t v_t^T)^T r_t;  S <- diag(w_t) S + k_t v_t^T            (S: dim x dim)
+//                   then per head o / rms(o), times a weight per element, times silu(gate)
+//   delta_rule:     S <- diag(g_t) S;  d = beta_t (v_t - S^T k_t);  S <- S + k_t d^T;  o_t = S^T q_t   (S: dim x vdim)
+//                   q, k made unit vectors per head (q also times dim^-1/2) on the way in; then per head o / rms(o),
+//                   times a weight per value channel, times sigmoid(gate)
+//
+// and what stands before them: token_shift (the five mixes of a token with the token before), lowrank_expand (the second
+// half of a low-rank map in float32 with the decays' nonlinearities), add_row_vector.
+//
+// The walk: a block per (segment, head). Thread (c, g) keeps rows g*DR .. g*DR+DR-1 of column c of the state in
+// registers; sums over the rows of a column go through shared memory (one barrier per sum, buffers in turn). Tokens come
+// in tiles of MS_TILE through shared memory; a tile's outputs are normed and written by the whole block. Every state
+// element is updated by one thread in the order of the tokens, so a request's result does not depend on how it was cut
+// into steps or what else the batch holds. Decays arrive as logarithms (float32, never positive) and are exponentiated here.
+#include "common.cuh"
+
+#define MS_TILE 16
+#define MS_MAX_THREADS 1024
+
+__device__ __forceinline__ float ms_load(const void* p, int dtype, size_t i) {
+    return dtype == TTB_DTYPE_BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i])
+                                   : reinterpret_cast<const float*>(p)[i];
+}
+__device__ __forceinline__ void ms_store(void* p, int dtype, size_t i, float v) {
+    if (dtype == TTB_DTYPE_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float*>(p)[i] = v;
+}
+__device__ __forceinline__ float ms_sigmoid(float v) { return 1.f / (1.f + expf(-v)); }
+
+// ---------------------------------------------------------------- token shift
+// out[t, s, c] = x[t, c] + (before[t, c] - x[t, c]) * mu[s, c]; before = the segment's token in front, or the request's
+// kept input for the segment's first token. The kept input is replaced later, by the walk.
+__global__ void __launch_bounds__(256)
+token_shift_kernel(const void* __restrict__ x, int dtype, int ldx, const float* __restrict__ mu, int mixes,
+                   const int* __restrict__ seg_of_token, const int* __restrict__ cu_seqlens, const int* __restrict__ slots,
+                   const void* __restrict__ kept, void* __restrict__ out, int tokens, int width) {
+    pdl_wait();
+    pdl_launch_dependents();
+    for (int t = blockIdx.x; t < tokens; t += gridDim.x) {
+        const int seg = seg_of_token[t];
+        const bool first = t == cu_seqlens[seg];
+        const size_t kept_row = (size_t)slots[seg] * width;
+        for (int c = threadIdx.x; c < width; c += blockDim.x) {
+            const float cur = ms_load(x, dtype, (size_t)t * ldx + c);
+            const float before = first ? ms_load(kept, dtype, kept_row + c) : ms_load(x, dtype, (size_t)(t - 1) * ldx + c);
+            const float diff = before - cur;
+            for (int s = 0; s < mixes; ++s)
+                ms_store(out, dtype, ((size_t)t * mixes + s) * width + c, fmaf(diff, mu[(size_t)s * width + c], cur));
+        }
+    }
+}
+
+TTB_EXPORT int ttb_token_shift(const void* x, int dtype, int ldx, const float* mu, int mixes, const int* seg_of_token,
+                               const int* cu_seqlens, const int* slots, const void* kept, void* out, int tokens, int width,
+                               cudaStream_t stream) {
+    if (tokens == 0) return TTB_OK;
+    if (!x || !mu || !seg_of_token || !cu_seqlens || !slots || !kept || !out || mixes < 1 || width < 1) return TTB_ERR_ARGUMENT;
+    if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    ttb_launch(token_shift_kernel, tokens < 148 * 8 ? tokens : 148 * 8, 256, 0, stream, x, dtype, ldx, mu, mixes, seg_of_token,
+               cu_seqlens, slots, kept, out, tokens, width);
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- the second half of a low-rank map
+// out[t, n] = f(sum_r act(in[t, r]) W[n, r] + bias[n]), float32 arithmetic; in float32 [tokens, ld_in]; W [N, rank] of
+// the compute type. act: 0 none, 1 tanh. f: 0 z; 1 -exp(z); 2 -rate[n / (N / heads)] * softplus(z).
+#define LR_TOKENS 8
+__global__ void __launch_bounds__(256)
+lowrank_expand_kernel(const float* __restrict__ in, int ld_in, const void* __restrict__ w, int w_dtype,
+                      const float* __restrict__ bias, const float* __restrict__ rate, int per_head, int act, int f,
+                      float* __restrict__ out, int tokens, int N, int rank) {
+    extern __shared__ float lr_in[];                 // [LR_TOKENS, rank]
+    pdl_wait();
+    pdl_launch_dependents();
+    const int t0 = blockIdx.x * LR_TOKENS, nt = min(LR_TOKENS, tokens - t0);
+    for (int i = threadIdx.x; i < LR_TOKENS * rank; i += blockDim.x) {
+        const int tt = i / rank, r = i - tt * rank;
+        float v = tt < nt ? in[(size_t)(t0 + tt) * ld_in + r] : 0.f;
+        lr_in[i] = act == 1 ? tanhf(v) : v;
+    }
+    __syncthreads();
+    for (int n = blockIdx.y * blockDim.x + threadIdx.x; n < N; n += gridDim.y * blockDim.x) {
+        float acc[LR_TOKENS];
+#pragma unroll
+        for (int tt = 0; tt < LR_TOKENS; ++tt) acc[tt] = 0.f;
+        for (int r = 0; r < rank; ++r) {
+            const float wv = ms_load(w, w_dtype, (size_t)n * rank + r);
+#pragma unroll
+            for (int tt = 0; tt < LR_TOKENS; ++tt) acc[tt] = fmaf(lr_in[tt * rank + r], wv, acc[tt]);
+        }
+        const float b = bias != nullptr ? bias[n] : 0.f;
+        const float rt = f == 2 ? rate[n / per_head] : 0.f;
+#pragma unroll
+        for (int tt = 0; tt < LR_TOKENS; ++tt) {
+            if (tt < nt) {
+                float z = acc[tt] + b;
+                if (f == 1) z = -expf(z);
+                else if (f == 2) z = -rt * (z > 20.f ? z : log1pf(expf(z)));
+                out[(size_t)(t0 + tt) * N + n] = z;
+            }
+        }
+    }
+}
+
+TTB_EXPORT int ttb_lowrank_expand(const float* in, int ld_in, const void* w, int w_dtype, const float* bias, const float* rate,
+                                  int heads, int act, int f, float* out, int tokens, int N, int rank, cudaStream_t stream) {
+    if (tokens == 0 || N == 0) return TTB_OK;
+    if (!in || !w || !out || rank < 1 || (f == 2 && (!rate || heads < 1 || N % heads))) return TTB_ERR_ARGUMENT;
+    if (w_dtype != TTB_DTYPE_BF16 && w_dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    if (act < 0 || act > 1 || f < 0 || f > 2) return TTB_ERR_UNSUPPORTED;
+    const size_t smem = (size_t)LR_TOKENS * rank * sizeof(float);
+    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
+    const int by = (N + 255) / 256;
+    dim3 grid((tokens + LR_TOKENS - 1) / LR_TOKENS, by > 64 ? 64 : by);
+    ttb_launch(lowrank_expand_kernel, grid, 256, smem, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
+               out, tokens, N, rank);
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- x += vector, row by row
+__global__ void add_row_vector_kernel(void* __restrict__ x, int dtype, int ld, const float* __restrict__ vec, int rows, int width) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t total = (size_t)rows * width;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / width, c = i - r * width;
+        ms_store(x, dtype, r * ld + c, ms_load(x, dtype, r * ld + c) + vec[c]);
+    }
+}
+
+TTB_EXPORT int ttb_add_row_vector(void* x, int dtype, int ld, const float* vec, int rows, int width, cudaStream_t stream) {
+    if (rows == 0 || width == 0) return TTB_OK;
+    if (!x || !vec) return TTB_ERR_ARGUMENT;
+    if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    const size_t total = (size_t)rows * width;
+    const int blocks = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+    ttb_launch(add_row_vector_kernel, blocks, 256, 0, stream, x, dtype, ld, vec, rows, width);
+    return ttb_launch_status();
+}
+
+// ---------------------------------------------------------------- the walks
+struct MsArgs {
+    // shifted_state: a = r, b = k, c = v, gate = silu gate (all [T, heads * dim] of the compute type, row strides below)
+    // delta_rule:    a = q, b = k (heads of kv_heads, [T, .] columns of `conv`), c = v; gate float32 [T, heads * vdim]
+    const void* a; const void* b; const void* c; const void* gate;
+    long long ld_a, ld_b, ld_c, ld_gate;
+    int dtype;                   // of a, b, c, out, kept
+    int gate_dtype;
+    const float* log_decay;      // [T, heads * dim]
+    const float* bonus;          // shifted_state: [heads, dim]
+    const float* beta; int ld_beta;   // delta_rule: logits [T, heads] with a row stride
+    const float* norm_w;         // shifted_state: [heads * dim]; delta_rule: [vdim]
+    float eps;
+    const int* cu_seqlens; const int* slots;
+    float* state;                // [slots, heads, D, V]
+    void* kept;                  // shifted_state: [slots, width]; delta_rule: [slots, taps - 1, channels]
+    const void* raw; long long ld_raw;   // what the kept inputs are refreshed from: x [T, width], or the convolutions' inputs [T, channels]
+    int width;                   // shifted_state: the model width; delta_rule: channels
+    int taps;
+    void* out;                   // [T, heads * V]
+    int heads, kv_heads, D, V, R, write;
+};
+
+template <int DR, bool DELTA>
+__global__ void __launch_bounds__(DR == 64 ? MS_MAX_THREADS : 512)
+matrix_state_walk_kernel(const MsArgs p) {
+    extern __shared__ __align__(16) float ms_smem[];
+    const int D = p.D, V = p.V, R = p.R;
+    float* sa = ms_smem;                       // [TILE, D]  r or q
+    float* sb = sa + MS_TILE * D;              // [TILE, D]  k
+    float* sw = sb + MS_TILE * D;              // [TILE, D]  decay
+    float* sc = sw + MS_TILE * D;              // [TILE, V]  v
+    float* so = sc + MS_TILE * V;              // [TILE, V]  outputs
+    float* part = so + MS_TILE * V;            // [2, R, V]
+    float* sbeta = part + 2 * R * V;           // [TILE]
+    float* sbonus = sbeta + MS_TILE;           // [D]
+    float* sscale = sbonus + D;                // [TILE, 2]: unit-norm factors of q and k (delta), then the outputs' norm
+    pdl_wait();
+    pdl_launch_dependents();
+    const int seg = blockIdx.x, head = blockIdx.y;
+    const int kvh = DELTA ? head / (p.heads / p.kv_heads) : head;
+    const int tid = threadIdx.x, nthreads = blockDim.x;
+    const int col = tid % V, grp = tid / V;
+    const bool active = grp < R;
+    const int row0 = grp * DR;
+    const int start = p.cu_seqlens[seg], len = p.cu_seqlens[seg + 1] - start;
+    const int slot = p.slots[seg];
+    float* state = p.state + ((size_t)slot * p.heads + head) * D * V;
+    float S[DR];
+#pragma unroll
+    for (int i = 0; i < DR; ++i) S[i] = (active && row0 + i < D) ? state[(size_t)(row0 + i) * V + col] : 0.f;
+    if (!DELTA)
+        for (int d = tid; d < D; d += nthreads) sbonus[d] = p.bonus[(size_t)head * D + d];
+    const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
+    int turn = 0;
+    for (int t0 = 0; t0 < len; t0 += MS_TILE) {
+        const int nt = min(MS_TILE, len - t0);
+        __syncthreads();                       // the tile before is written out
+        for (int i = tid; i < nt * D; i += nthreads) {
+            const int tt = i / D, d = i - tt * D;
+            const size_t t = (size_t)(start + t0 + tt);
+            sa[i] = ms_load(p.a, p.dtype, t * p.ld_a + (size_t)kvh * D + d);
+            sb[i] = ms_load(p.b, p.dtype, t * p.ld_b + (size_t)kvh * D + d);
+            sw[i] = expf(p.log_decay[t * ((size_t)p.heads * D) + (size_t)head * D + d]);
+        }
+        for (int i = tid; i < nt * V; i += nthreads) {
+            const int tt = i / V, c = i - tt * V;
+            sc[i] = ms_load(p.c, p.dtype, (size_t)(start + t0 + tt) * p.ld_c + (size_t)head * V + c);
+        }
+        if (DELTA) {
+            for (int tt = tid; tt < nt; tt += nthreads) sbeta[tt] = ms_sigmoid(p.beta[(size_t)(start + t0 + tt) * p.ld_beta + head]);
+            __syncthreads();
+            for (int i = warp; i < 2 * nt; i += nwarps) {          // unit vectors: a warp per (token, q or k)
+                const float* src = (i & 1 ? sb : sa) + (i >> 1) * D;
+                float s = 0.f;
+                for (int d = lane; d < D; d += 32) s = fmaf(src[d], src[d], s);
+                s = warp_sum(s);
+                if (lane == 0) sscale[i] = (1.f / sqrtf(s + 1e-6f)) * (i & 1 ? 1.f : 1.f / sqrtf((float)D));
+            }
+            __syncthreads();
+            for (int i = tid; i < nt * D; i += nthreads) {
+                const int tt = i / D;
+                sa[i] *= sscale[2 * tt];
+                sb[i] *= sscale[2 * tt + 1];
+            }
+        }
+        __syncthreads();
+        for (int tt = 0; tt < nt; ++tt) {
+            const float* a = sa + tt * D + row0;
+            const float* b = sb + tt * D + row0;
+            const float* w = sw + tt * D + row0;
+            float* mine = part + (size_t)turn * R * V;
+            if (DELTA) {
+                float s = 0.f;
+                if (active) {
+#pragma unroll
+                    for (int i = 0; i < DR; ++i)
+                        if (row0 + i < D) { S[i] *= w[i]; s = fmaf(S[i], b[i], s); }
+                    mine[grp * V + col] = s;
+                }
+                __syncthreads();
+                float got = 0.f;
+                for (int g = 0; g < R; ++g) got += mine[g * V + col];
+                const float d = sbeta[tt] * (sc[tt * V + col] - got);
+                turn ^= 1;
+                mine = part + (size_t)turn * R * V;
+                s = 0.f;
+                if (active) {
+#pragma unroll
+                    for (int i = 0; i < DR; ++i)
+                        if (row0 + i < D) { S[i] = fmaf(b[i], d, S[i]); s = fmaf(S[i], a[i], s); }
+                    mine[grp * V + col] = s;
+                }
+                __syncthreads();
+                if (grp == 0) {
+                    float o = 0.f;
+                    for (int g = 0; g < R; ++g) o += mine[g * V + col];
+                    so[tt * V + col] = o;
+                }
+                turn ^= 1;
+            } else {
+                const float vc = sc[tt * V + col];
+                float s = 0.f;
+                if (active) {
+#pragma unroll
+                    for (int i = 0; i < DR; ++i) {
+                        if (row0 + i < D) {
+                            const float kv = b[i] * vc;
+                            s = fmaf(a[i], fmaf(sbonus[row0 + i], kv, S[i]), s);
+                            S[i] = fmaf(w[i], S[i], kv);
+                        }
+                    }
+                    mine[grp * V + col] = s;
+                }
+                __syncthreads();
+                if (grp == 0) {
+                    float o = 0.f;
+                    for (int g = 0; g < R; ++g) o += mine[g * V + col];
+                    so[tt * V + col] = o;
+                }
+                turn ^= 1;
+            }
+        }
+        __syncthreads();
+        // the tile's outputs: per head o / rms(o), a weight, the gate
+        for (int tt = warp; tt < nt; tt += nwarps) {
+            float s = 0.f;
+            for (int c = lane; c < V; c += 32) s = fmaf(so[tt * V + c], so[tt * V + c], s);
+            s = warp_sum(s);
+            if (lane == 0) sscale[tt] = rsqrtf(s / (float)V + p.eps);
+        }
+        __syncthreads();
+        for (int i = tid; i < nt * V; i += nthreads) {
+            const int tt = i / V, c = i - tt * V;
+            const size_t t = (size_t)(start + t0 + tt);
+            const float g = ms_load(p.gate, p.gate_dtype, t * p.ld_gate + (size_t)head * V + c);
+            const float weight = DELTA ? p.norm_w[c] : p.norm_w[(size_t)head * V + c];
+            const float gated = DELTA ? ms_sigmoid(g) : g * ms_sigmoid(g);
+            ms_store(p.out, p.dtype, t * ((size_t)p.heads * V) + (size_t)head * V + c, so[i] * sscale[tt] * weight * gated);
+        }
+    }
+    if (!p.write || len == 0) return;
+#pragma unroll
+    for (int i = 0; i < DR; ++i)
+        if (active && row0 + i < D) state[(size_t)(row0 + i) * V + col] = S[i];
+    if (!DELTA) {
+        // the kept input becomes the segment's last token; the heads share the columns between them
+        const int c0 = (int)((long long)p.width * head / p.heads), c1 = (int)((long long)p.width * (head + 1) / p.heads);
+        for (int c = c0 + tid; c < c1; c += nthreads)
+            ms_store(p.kept, p.dtype, (size_t)slot * p.width + c, ms_load(p.raw, p.dtype, (size_t)(start + len - 1) * p.ld_raw + c));
+        return;
+    }
+    // the convolutions' kept inputs for the channels this head owns: its values, and q and k of its key head if it is
+    // that head's first. A thread per channel walks the kept rows oldest first, so a short segment shifts the old rows
+    // down before it overwrites them.
+    const int keep = p.taps - 1;
+    if (keep <= 0) return;
+    const int qk = p.kv_heads * D;
+    const bool owns_qk = head % (p.heads / p.kv_heads) == 0;
+    const int count = V + (owns_qk ? 2 * D : 0);
+    for (int i = tid; i < count; i += nthreads) {
+        int ch;
+        if (i < V) ch = 2 * qk + head * V + i;
+        else if (i < V + D) ch = kvh * D + (i - V);
+        else ch = qk + kvh * D + (i - V - D);
+        for (int j = 0; j < keep; ++j) {
+            const int local = len - keep + j;
+            float v;
+            if (local >= 0) v = ms_load(p.raw, p.dtype, (size_t)(start + local) * p.ld_raw + ch);
+            else v = ms_load(p.kept, p.dtype, ((size_t)slot * keep + (keep + local)) * p.width + ch);
+            ms_store(p.kept, p.dtype, ((size_t)slot * keep + j) * p.width + ch, v);
+        }
+    }
+}
+
+template <bool DELTA>
+static int ms_launch(MsArgs& p, int segments, cudaStream_t stream) {
+    const int D = p.D, V = p.V;
+    if (D < 1 || V < 1 || V > MS_MAX_THREADS || p.heads < 1 || p.heads > 65535) return TTB_ERR_UNSUPPORTED;
+    // the fewest rows a thread that still lets a column's row groups fit one block, and at most 512 threads where that works
+    int DR = 8;
+    while (DR < 64 && V * ((D + DR - 1) / DR) > 512) DR *= 2;
+    const int R = (D + DR - 1) / DR;
+    if (V * R > MS_MAX_THREADS) return TTB_ERR_UNSUPPORTED;
+    p.R = R;
+    int threads = (V * R + 31) / 32 * 32;
+    if (threads < 64) threads = 64;
+    const size_t smem = ((size_t)MS_TILE * (3 * D + 2 * V) + 2 * (size_t)R * V + MS_TILE + D + 2 * MS_TILE) * sizeof(float);
+    if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    dim3 grid(segments, p.heads);
+#define MS_GO(DRV)                                                                                                   \
+    do {                                                                                                             \
+        static TtbOncePerDevice once;                                                                                \
+        if (smem > 48 * 1024 && once.pending()) {                                                                    \
+            cudaFuncSetAttribute(matrix_state_walk_kernel<DRV, DELTA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+            once.mark();                                                                                             \
+        }                                                                                                            \
+        ttb_launch(matrix_state_walk_kernel<DRV, DELTA>, grid, threads, smem, stream, p);                            \
+    } while (0)
+    if (DR == 8) MS_GO(8); else if (DR == 16) MS_GO(16); else if (DR == 32) MS_GO(32); else MS_GO(64);
+#undef MS_GO
+    return ttb_launch_status();
+}
+
+// rkvg: r, k, v and the gate [T, heads * dim] each, of the compute type, with a common row stride `ld` and `which` elements
+// between one and the next. log_decay float32 [T, heads * dim]; bonus float32 [heads, dim]; norm_w float32 [heads * dim].
+// state float32 [slots, heads, dim, dim]; kept [slots, width]: the request's last input, refreshed from x [T, ldx].
+TTB_EXPORT int ttb_shifted_state(const void* rkvg, int dtype, long long ld, long long which, const float* log_decay,
+                                 const float* bonus, const float* norm_w, float eps, const void* x, long long ldx, int width,
+                                 const int* cu_seqlens, const int* slots, float* state, void* kept, void* out, int segments,
+                                 int heads, int dim, int write, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!rkvg || !log_decay || !bonus || !norm_w || !x || !cu_seqlens || !slots || !state || !kept || !out) return TTB_ERR_ARGUMENT;
+    if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    const size_t el = dtype == TTB_DTYPE_BF16 ? 2 : 4;
+    MsArgs p = {};
+    p.a = rkvg; p.b = (const char*)rkvg + which * el; p.c = (const char*)rkvg + 2 * which * el; p.gate = (const char*)rkvg + 3 * which * el;
+    p.ld_a = p.ld_b = p.ld_c = p.ld_gate = ld;
+    p.dtype = p.gate_dtype = dtype;
+    p.log_decay = log_decay; p.bonus = bonus; p.norm_w = norm_w; p.eps = eps;
+    p.cu_seqlens = cu_seqlens; p.slots = slots; p.state = state; p.kept = kept; p.raw = x; p.ld_raw = ldx; p.width = width;
+    p.taps = 2; p.out = out; p.heads = heads; p.kv_heads = heads; p.D = dim; p.V = dim; p.write = write;
+    return ms_launch<false>(p, segments, stream);
+}
+
+// conv [T, q | k | v] after the convolutions and their silu (q, k: kv_heads * dim; v: heads * vdim), row stride ld_conv;
+// raw: the convolutions' inputs in the same layout; beta float32 logits [T, heads] (row stride ld_beta); log_decay float32
+// [T, heads * dim]; gate float32 logits [T, heads * vdim]; norm_w float32 [vdim]. state float32 [slots, heads, dim, vdim];
+// kept [slots, taps - 1, channels].
+TTB_EXPORT int ttb_delta_rule(const void* conv, int dtype, long long ld_conv, const void* raw, long long ld_raw,
+                              const float* beta, int ld_beta, const float* log_decay, const float* gate, const float* norm_w,
+                              float eps, const int* cu_seqlens, const int* slots, float* state, void* kept, void* out,
+                              int segments, int heads, int kv_heads, int dim, int vdim, int taps, int write, cudaStream_t stream) {
+    if (segments == 0) return TTB_OK;
+    if (!conv || !raw || !beta || !log_decay || !gate || !norm_w || !cu_seqlens || !slots || !state || !out || (taps > 1 && !kept))
+        return TTB_ERR_ARGUMENT;
+    if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
+    if (kv_heads < 1 || heads % kv_heads) return TTB_ERR_UNSUPPORTED;
+    const size_t el = dtype == TTB_DTYPE_BF16 ? 2 : 4;
+    const long long qk = (long long)kv_heads * dim;
+    MsArgs p = {};
+    p.a = conv; p.b = (const char*)conv + qk * el; p.c = (const char*)conv + 2 * qk * el; p.gate = gate;
+    p.ld_a = p.ld_b = p.ld_c = ld_conv; p.ld_gate = (long long)heads * vdim;
+    p.dtype = dtype; p.gate_dtype = TTB_DTYPE_F32;
+    p.log_decay = log_decay; p.beta = beta; p.ld_beta = ld_beta; p.norm_w = norm_w; p.eps = eps;
+    p.cu_seqlens = cu_seqlens; p.slots = slots; p.state = state; p.kept = kept; p.raw = raw; p.ld_raw = ld_raw;
+    p.width = (int)(2 * qk + (long long)heads * vdim); p.taps = taps; p.out = out;
+    p.heads = heads; p.kv_heads = kv_heads; p.D = dim; p.V = vdim; p.write = write;
+    return ms_launch<true>(p, segments, stream);
+}

@@ -23,7 +23,7 @@ template <typename T, int TPB>
 __global__ void __launch_bounds__(TPB == 1 ? 1024 : 512, TPB == 1 ? 1 : 2)       // many tokens: two blocks an SM
 route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_router, int width, int experts, int top,
                  int shared, int* __restrict__ choice, float* __restrict__ weight, float* __restrict__ shared_gate,
-                 int tokens, int scores) {
+                 int tokens, int scores, const float* __restrict__ correction, float out_scale, float floor_) {
     extern __shared__ __align__(16) float rt_smem[];
     const int wpad = (width + 3) & ~3;
     float* h = rt_smem;                                   // [TPB, wpad]
@@ -106,7 +106,8 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
             float best_z = -INFINITY;
             int best = 0x7fffffff;
             for (int e = lane; e < experts; e += 32) {
-                const float v = tk[e] ? -INFINITY : zt[e];
+                // scores 2: the choice goes by the expert's own sigmoid score plus its correction
+                const float v = tk[e] ? -INFINITY : (scores == 2 ? 1.f / (1.f + expf(-zt[e])) + correction[e] : zt[e]);
                 if (!tk[e] && (best == 0x7fffffff || v > best_z)) { best = e; best_z = v; }
             }
 #pragma unroll
@@ -118,7 +119,8 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
             if (lane == 0) tk[best] = 1;
             __syncwarp();
             if (j == 0) best_first = best_z;
-            const float p = scores == 1 ? 1.f / (1.f + expf(-best_z)) : expf(best_z - best_first);
+            const float p = scores == 2 ? 1.f / (1.f + expf(-zt[best]))
+                                        : (scores == 1 ? 1.f / (1.f + expf(-best_z)) : expf(best_z - best_first));
             denom += p;
             if (lane == 0) {
                 choice[(size_t)t * top + j] = best;
@@ -128,6 +130,8 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
         __syncwarp();                                      // lane 0's weights are visible to the warp
         if (scores == 0)
             for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] /= denom;
+        if (scores == 2)      // the chosen scores without their corrections, over their sum, times the router's scale
+            for (int j = lane; j < top; j += 32) weight[(size_t)t * top + j] = weight[(size_t)t * top + j] / (denom + floor_) * out_scale;
         if (shared && lane == 0) shared_gate[t] = 1.f / (1.f + expf(-zt[experts]));
     }
 }
@@ -135,7 +139,7 @@ route_top_kernel(const T* __restrict__ x, int ldx, const float* __restrict__ w_r
 template <typename T, int TPB>
 static int route_top_launch(const void* x, int ldx, const float* w_router, int tokens, int width, int experts, int top,
                             int shared, int* choice, float* weight, float* shared_gate, int threads, int scores,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const float* correction = nullptr, float out_scale = 1.f, float floor_ = 0.f) {
     const size_t smem = ((size_t)TPB * (((width + 3) & ~3) + 2 * experts + 1)) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     static TtbOncePerDevice once;
@@ -144,17 +148,18 @@ static int route_top_launch(const void* x, int ldx, const float* w_router, int t
         once.mark();
     }
     ttb_launch(route_top_kernel<T, TPB>, (tokens + TPB - 1) / TPB, threads, smem, stream, (const T*)x, ldx, w_router, width,
-               experts, top, shared, choice, weight, shared_gate, tokens, scores);
+               experts, top, shared, choice, weight, shared_gate, tokens, scores, correction, out_scale, floor_);
     return ttb_launch_status();
 }
 
-// scores 0: the chosen experts' weights are the softmax over their logits; 1: each one's own sigmoid(logit), as it is.
-TTB_EXPORT int ttb_route_top_scored(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
-                                    int top, int shared, int* choice, float* weight, float* shared_gate, int scores,
-                                    cudaStream_t stream) {
+// scores 0: the chosen experts' weights are the softmax over their logits; 1: each one's own sigmoid(logit), as it is;
+// 2: chosen by sigmoid(logit) + correction[e], weighted by sigmoid(logit) / (sum over the chosen + floor) * out_scale.
+TTB_EXPORT int ttb_route_top_corrected(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
+                                       int top, int shared, int* choice, float* weight, float* shared_gate, int scores,
+                                       const float* correction, float out_scale, float floor_, cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
-    if (scores != 0 && scores != 1) return TTB_ERR_UNSUPPORTED;
-    if (!x || !w_router || !choice || !weight || (shared && !shared_gate)) return TTB_ERR_ARGUMENT;
+    if (scores < 0 || scores > 2) return TTB_ERR_UNSUPPORTED;
+    if (!x || !w_router || !choice || !weight || (shared && !shared_gate) || (scores == 2 && !correction)) return TTB_ERR_ARGUMENT;
     if (experts < 1 || experts > RT_MAX_EXPERTS || top < 1 || top > experts) return TTB_ERR_UNSUPPORTED;
     if ((width & 3) == 0 && !aligned16(w_router)) return TTB_ERR_ARGUMENT;
     const int rows = experts + (shared ? 1 : 0);
@@ -164,12 +169,20 @@ TTB_EXPORT int ttb_route_top_scored(const void* x, int dtype, int ldx, const flo
     const int most = many ? 16 : 32;
     const int threads = 32 * (rows < 4 ? 4 : (rows > most ? most : rows));
 #define RT_LAUNCH(T)                                                                                                 \
-    (many ? route_top_launch<T, 8>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream) \
-          : route_top_launch<T, 1>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream))
+    (many ? route_top_launch<T, 8>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream, correction, out_scale, floor_) \
+          : route_top_launch<T, 1>(x, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, threads, scores, stream, correction, out_scale, floor_))
     if (dtype == TTB_DTYPE_BF16) return RT_LAUNCH(__nv_bfloat16);
     if (dtype == TTB_DTYPE_F32) return RT_LAUNCH(float);
 #undef RT_LAUNCH
     return TTB_ERR_UNSUPPORTED;
+}
+
+TTB_EXPORT int ttb_route_top_scored(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,
+                                    int top, int shared, int* choice, float* weight, float* shared_gate, int scores,
+                                    cudaStream_t stream) {
+    if (scores != 0 && scores != 1) return TTB_ERR_UNSUPPORTED;
+    return ttb_route_top_corrected(x, dtype, ldx, w_router, tokens, width, experts, top, shared, choice, weight, shared_gate, scores,
+                                   nullptr, 1.f, 0.f, stream);
 }
 
 TTB_EXPORT int ttb_route_top(const void* x, int dtype, int ldx, const float* w_router, int tokens, int width, int experts,

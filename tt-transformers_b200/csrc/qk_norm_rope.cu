@@ -19,7 +19,8 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
                           const float* __restrict__ q_weight, const float* __restrict__ k_weight, float eps,
                           const float* __restrict__ inv_freq, int rotary_dim, int heads, int kv_heads, int dim, int vdim,
                           T* __restrict__ key_pages, T* __restrict__ value_pages, const int* __restrict__ block_table,
-                          int table_width, int page_size, int num_pages, int write_kv, int* __restrict__ status) {
+                          int table_width, int page_size, int num_pages, int write_kv, int* __restrict__ status,
+                          const float* __restrict__ bias, float temp_coef, int temp_every) {
     extern __shared__ float qn_rows[];         // [warps][dim]
     pdl_wait();
     pdl_launch_dependents();
@@ -54,22 +55,33 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
     }
     if (!is_q && !is_k) {                       // a value head: a copy
         const T* src = qkv + (size_t)t * ld + (size_t)(heads + kv_heads) * dim + (size_t)g * vdim;
-        if (dst_page != nullptr)
-            for (int d = lane; d < vdim; d += 32) dst_page[d] = src[d];
+        if (dst_page != nullptr) {
+            if (bias != nullptr) {
+                const float* b = bias + (size_t)(heads + kv_heads) * dim + (size_t)g * vdim;
+                for (int d = lane; d < vdim; d += 32) dst_page[d] = from_float<T>(to_float(src[d]) + b[d]);
+            } else {
+                for (int d = lane; d < vdim; d += 32) dst_page[d] = src[d];
+            }
+        }
         return;
     }
     T* row = qkv + (size_t)t * ld + (size_t)(is_q ? g : heads + g) * dim;
     const float* weight = is_q ? q_weight : k_weight;
+    const float* row_bias = bias != nullptr ? bias + (size_t)(is_q ? g : heads + g) * dim : nullptr;
     float sumsq = 0.f;
     for (int d = lane; d < dim; d += 32) {
-        const float v = to_float(row[d]);
+        const float v = to_float(row[d]) + (row_bias != nullptr ? row_bias[d] : 0.f);
         qn_row[d] = v;
         sumsq += v * v;
     }
+    // a query's temperature: 1 + c ln(floor((position + 1) / n) + 1)
+    const float temperature = (is_q && temp_coef != 0.f) ? 1.f + temp_coef * logf((float)((pos + 1) / temp_every) + 1.f) : 1.f;
     if (weight != nullptr) {
         sumsq = warp_sum(sumsq);
-        const float scale = 1.f / sqrtf(sumsq / (float)dim + eps);
+        const float scale = temperature / sqrtf(sumsq / (float)dim + eps);
         for (int d = lane; d < dim; d += 32) qn_row[d] = qn_row[d] * scale * weight[d];
+    } else if (temperature != 1.f) {
+        for (int d = lane; d < dim; d += 32) qn_row[d] *= temperature;
     }
     __syncwarp();
     const int half = rotary_dim / 2;
@@ -87,11 +99,14 @@ qk_norm_rope_write_kernel(T* __restrict__ qkv, int ld, const int* __restrict__ p
     }
 }
 
-TTB_EXPORT int ttb_qk_norm_rope_write(void* qkv, int dtype, int ld, const int* positions, const int* seg_of_token,
+// bias: float32 [heads * dim | kv_heads * dim | kv_heads * vdim] added to q, k and v before anything else (or null);
+// temp_coef, temp_every: the queries' temperature by position (coef 0: none).
+TTB_EXPORT int ttb_qk_norm_rope_write_ext(void* qkv, int dtype, int ld, const int* positions, const int* seg_of_token,
                                       const float* q_weight, const float* k_weight, float eps, const float* inv_freq,
                                       int rotary_dim, int tokens, int heads, int kv_heads, int dim, int vdim, void* key_pages,
                                       void* value_pages, const int* block_table, int table_width, int page_size, int num_pages,
-                                      int write_kv, int* status, cudaStream_t stream) {
+                                      int write_kv, int* status, const float* bias, float temp_coef, int temp_every,
+                                      cudaStream_t stream) {
     if (tokens == 0) return TTB_OK;
     if (!qkv || !positions || !seg_of_token || !status) return TTB_ERR_ARGUMENT;
     if (write_kv && (!key_pages || !value_pages || !block_table || page_size < 1)) return TTB_ERR_ARGUMENT;
@@ -103,13 +118,24 @@ TTB_EXPORT int ttb_qk_norm_rope_write(void* qkv, int dtype, int ld, const int* p
     if (dtype == TTB_DTYPE_BF16)
         ttb_launch(qk_norm_rope_write_kernel<__nv_bfloat16>, grid, QN_THREADS, smem, stream, (__nv_bfloat16*)qkv, ld, positions,
                    seg_of_token, q_weight, k_weight, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, (__nv_bfloat16*)key_pages,
-                   (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status);
+                   (__nv_bfloat16*)value_pages, block_table, table_width, page_size, num_pages, write_kv, status, bias, temp_coef,
+                   temp_every);
     else if (dtype == TTB_DTYPE_F32)
         ttb_launch(qk_norm_rope_write_kernel<float>, grid, QN_THREADS, smem, stream, (float*)qkv, ld, positions, seg_of_token,
                    q_weight, k_weight, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, (float*)key_pages, (float*)value_pages,
-                   block_table, table_width, page_size, num_pages, write_kv, status);
+                   block_table, table_width, page_size, num_pages, write_kv, status, bias, temp_coef, temp_every);
     else return TTB_ERR_UNSUPPORTED;
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_qk_norm_rope_write(void* qkv, int dtype, int ld, const int* positions, const int* seg_of_token,
+                                      const float* q_weight, const float* k_weight, float eps, const float* inv_freq,
+                                      int rotary_dim, int tokens, int heads, int kv_heads, int dim, int vdim, void* key_pages,
+                                      void* value_pages, const int* block_table, int table_width, int page_size, int num_pages,
+                                      int write_kv, int* status, cudaStream_t stream) {
+    return ttb_qk_norm_rope_write_ext(qkv, dtype, ld, positions, seg_of_token, q_weight, k_weight, eps, inv_freq, rotary_dim, tokens,
+                                      heads, kv_heads, dim, vdim, key_pages, value_pages, block_table, table_width, page_size,
+                                      num_pages, write_kv, status, nullptr, 0.f, 1, stream);
 }
 
 // ---------------------------------------------------------------- the norm over the whole projection

@@ -120,7 +120,7 @@ TTB_EXPORT int ttb_mean_rmsnorm_pair(const void* a, const void* b, int dtype, co
 }
 
 // ---------------------------------------------------------------- activations on a product's output
-// kind 0: silu(g) * u, 1: gelu_tanh(g) * u over [rows, gate | up] -> [rows, cols]; 2: relu(z)^2, 3: the erf GELU over [rows, cols].
+// kind 0: silu(g) * u, 1: gelu_tanh(g) * u, 4: relu(g) * u over [rows, gate | up] -> [rows, cols]; 2: relu(z)^2, 3: the erf GELU over [rows, cols].
 __device__ __forceinline__ float gelu_tanh(float z) {
     return 0.5f * z * (1.f + tanhf(0.7978845608028654f * (z + 0.044715f * z * z * z)));
 }
@@ -141,7 +141,7 @@ __global__ void activation_kernel(const void* __restrict__ in, int in_dtype, int
             v = 0.5f * g * (1.f + erff(g * 0.70710678118654752f));
         } else {
             const float u = sn_load(in, in_dtype, r * in_stride + cols + c);
-            v = (kind == 0 ? g / (1.f + expf(-g)) : gelu_tanh(g)) * u;
+            v = (kind == 0 ? g / (1.f + expf(-g)) : (kind == 4 ? fmaxf(g, 0.f) : gelu_tanh(g))) * u;
         }
         sn_store(out, out_dtype, i, v);
     }
@@ -150,7 +150,7 @@ __global__ void activation_kernel(const void* __restrict__ in, int in_dtype, int
 TTB_EXPORT int ttb_activation(const void* in, int in_dtype, int in_stride, void* out, int out_dtype, int rows, int cols, int kind,
                               cudaStream_t stream) {
     if (rows == 0 || cols == 0) return TTB_OK;
-    if (!in || !out || kind < 0 || kind > 3) return TTB_ERR_ARGUMENT;
+    if (!in || !out || kind < 0 || kind > 4) return TTB_ERR_ARGUMENT;
     const size_t total = (size_t)rows * cols;
     const int blocks = (int)((total + 255) / 256 > 148 * 16 ? 148 * 16 : (total + 255) / 256);
     ttb_launch(activation_kernel, blocks, 256, 0, stream, in, in_dtype, in_stride, out, out_dtype, rows, cols, kind);

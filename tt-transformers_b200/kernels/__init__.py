@@ -103,7 +103,10 @@ class CudaKernels:
                      "ttb_paged_attention_mma_ext", "ttb_lightning_chunks", "ttb_lightning_chunks_supports",
                      "ttb_recurrent_token", "ttb_add_dyntanh", "ttb_concat_cast", "ttb_qk_whole_norm_rope_write",
                      "ttb_route_top_scored", "ttb_moe_gemv_scaled", "ttb_gather_rows_scaled", "ttb_conv_silu",
-                     "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm", "ttb_state_space_token"):
+                     "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm", "ttb_state_space_token",
+                     "ttb_token_shift", "ttb_lowrank_expand", "ttb_add_row_vector", "ttb_shifted_state", "ttb_delta_rule",
+                     "ttb_add_layernorm_sum", "ttb_qk_norm_rope_write_ext", "ttb_paged_attention_generic_bias",
+                     "ttb_latent_prepare_ext", "ttb_latent_attention_generic_ext", "ttb_route_top_corrected"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -614,25 +617,72 @@ class CudaKernels:
             self._stream()), "add_layernorm")
         return out
 
+    LN_SUM_TERMS = 4
+
+    def add_layernorm_sum(self, residual, tensors, scales, row_term, norm, out_dtype):
+        """residual += sum_i scales[i] * tensors[i] + row_term[1] * row_term[0], in place and in float32 (each tensor
+        [rows, width], float32 or bfloat16, contiguous; scales None: all one; row_term (float32 vector [width], factor) or
+        None); then norm(residual) in out_dtype (None when norm is None). `norm` is a layer-norm part (weight, bias or
+        None, eps)."""
+        rows, width = residual.shape
+        if residual.dtype != torch.float32 or not residual.is_contiguous():
+            raise KernelError("the residual stream is float32 and contiguous")
+        tensors = list(tensors)
+        scales = [1.0] * len(tensors) if scales is None else [float(s) for s in scales]
+        for t in tensors:
+            if t.shape != residual.shape or not t.is_contiguous():
+                raise KernelError("add_layernorm_sum: every term must be contiguous and have the stream's shape")
+        out = None
+        while True:
+            now, tensors = tensors[:self.LN_SUM_TERMS], tensors[self.LN_SUM_TERMS:]
+            now_scales, scales = scales[:self.LN_SUM_TERMS], scales[self.LN_SUM_TERMS:]
+            last = not tensors
+            n = len(now)
+            ptrs = (ctypes.c_void_p * max(n, 1))(*[t.data_ptr() for t in now])
+            dtypes = (ctypes.c_int * max(n, 1))(*[_dtype_code(t.dtype) for t in now])
+            factors = (ctypes.c_float * max(n, 1))(*now_scales)
+            normed = last and norm is not None
+            if normed:
+                out = torch.empty(rows, width, dtype=out_dtype, device=self.device)
+            row = row_term if last else None
+            if n or row is not None or normed:
+                self._check(self.lib.ttb_add_layernorm_sum(
+                    self._p(residual), ptrs, dtypes, factors, n, self._p(row[0] if row is not None else None),
+                    ctypes.c_float(row[1] if row is not None else 0.0), self._p(norm.weight if normed else None),
+                    self._p(norm.bias if normed else None), ctypes.c_float(norm.eps if normed else 0.0), self._p(out),
+                    _dtype_code(out_dtype) if normed else 0, rows, width, self._stream()), "add_layernorm_sum")
+            if last:
+                return out
+
+    def add_row_vector(self, x, vector):
+        """x [rows, width] += vector (float32 [width]), in place."""
+        rows, width = x.shape
+        if x.stride(1) != 1 or vector.dtype != torch.float32 or vector.shape != (width,):
+            raise KernelError("add_row_vector: contiguous columns and a float32 vector of the row's width")
+        self._check(self.lib.ttb_add_row_vector(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(vector), rows, width,
+                                                self._stream()), "add_row_vector")
+        return x
+
     # ------------------------------------------------------------------ latent attention
     def latent_prepare(self, down, batch, q_rank, kv_rank, rot_dim, q_norm, kv_norm, eps, inv_freq, rotary_dim, view,
-                       write, out_dtype):
-        """down: float32 [T, >= q_rank + kv_rank + rot_dim]. Returns the RMS-normed query latent [T, q_rank]; writes
-        the RMS-normed key/value latent and the rotated shared key part into the tokens' page rows."""
+                       write, out_dtype, amplitude=1.0):
+        """down: float32 [T, >= q_rank + kv_rank + rot_dim]. Returns the RMS-normed query latent [T, q_rank] (None with
+        q_rank 0); writes the RMS-normed key/value latent and the rotated shared key part (cosines and sines times
+        `amplitude`) into the tokens' page rows."""
         tokens = down.shape[0]
         if down.dtype != torch.float32 or down.stride(1) != 1:
             raise KernelError("latent_prepare: the down projection must be float32, contiguous along its columns")
         write = bool(write and view is not None)
         if write and (view.rows.dtype != out_dtype or not view.rows.is_contiguous()):
             raise KernelError("latent_prepare: the cache rows must be contiguous and of the compute dtype")
-        cq = torch.empty(tokens, q_rank, dtype=out_dtype, device=self.device)
-        self._check(self.lib.ttb_latent_prepare(
+        cq = torch.empty(tokens, q_rank, dtype=out_dtype, device=self.device) if q_rank else None
+        self._check(self.lib.ttb_latent_prepare_ext(
             self._p(down), down.stride(0), q_rank, kv_rank, rot_dim, self._p(q_norm), self._p(kv_norm),
             ctypes.c_float(eps), self._p(inv_freq), int(rotary_dim), self._p(batch.positions), self._p(batch.seg_of_token),
             self._p(cq), self._p(view.rows if write else None), _dtype_code(out_dtype),
             self._p(view.block_table if write else None), view.block_table.shape[1] if write else 0,
             view.page_size if write else 1, view.rows.shape[0] if write else 0, 1 if write else 0, tokens,
-            self._p(self.status), self._stream()), "latent_prepare")
+            self._p(self.status), ctypes.c_float(amplitude), self._stream()), "latent_prepare")
         return cq
 
     MOE_TCGEN05_PAIRS = 1024     # from this many pairs on the experts' products run on the grouped tcgen05 kernel
@@ -660,22 +710,24 @@ class CudaKernels:
 
     LATENT_OUT_ROWS = 64         # up to this many tokens the end of the mixer (merge, W_uv, gate) is one kernel
 
-    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim):
-        """q_latent [T, H, latent], q_rot [T, H, extra] or None (rotated here by the tokens' positions); the cache
-        rows hold [latent | extra] per token. Returns the weighted sums of the latents [T, H, latent]."""
-        return self._latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, True)[0]
+    def latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, amplitude=1.0, window="view"):
+        """q_latent [T, H, latent], q_rot [T, H, extra] or None (rotated here by the tokens' positions, cosines and sines
+        times `amplitude`); the cache rows hold [latent | extra] per token. `window`: what a query sees ("view": what the
+        cache keeps). Returns the weighted sums of the latents [T, H, latent]."""
+        return self._latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, True, amplitude, window)[0]
 
-    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate):
+    def latent_attention_out(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, w_uv, gate, amplitude=1.0,
+                             window="view"):
         """Attention over the latents, then per head W_uv [H, vdim, latent] and the gate (float32 logits [T, H] or
         [T, H * vdim], or None) -> [T, H * vdim]. For a handful of tokens the key splits' merge, the per-head
         product and the gate are one kernel."""
         T, H, R = q_latent.shape
         V = w_uv.shape[1]
         if T > self.LATENT_OUT_ROWS or R * 4 > 48 * 1024:
-            mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim)
+            mixed = self.latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, amplitude, window)
             return self.gate_heads(self.heads_linear(mixed, w_uv), gate)
         mixed, partial_o, partial_ml, splits = self._latent_attention(q_latent, q_rot, batch, view, scale, sinks, inv_freq,
-                                                                      rotary_dim, False)
+                                                                      rotary_dim, False, amplitude, window)
         return self.latent_out(mixed if splits == 1 else None, partial_o, partial_ml, splits, w_uv, gate, T, H, R)
 
     def latent_out(self, mixed, partial_o, partial_ml, splits, w_uv, gate, T, H, R):
@@ -698,10 +750,12 @@ class CudaKernels:
             V, self._stream()), "latent_out")
         return res
 
-    def _latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, merge):
+    def _latent_attention(self, q_latent, q_rot, batch, view, scale, sinks, inv_freq, rotary_dim, merge, amplitude=1.0,
+                          window="view"):
         """-> (weighted sums [T, H, latent], partial sums, their maxima and sums, number of key splits); with merge
         False and more than one split the first is not filled in and the partial results are the caller's to merge."""
         T, H, R = q_latent.shape
+        window = view.window if window == "view" else window
         if R != view.latent or q_latent.dtype != view.rows.dtype or q_latent.stride(2) != 1:
             raise KernelError("latent_attention: the queries do not fit the cache rows")
         if (q_rot is None) != (view.extra == 0) or (q_rot is not None and (q_rot.shape[2] != view.extra or q_rot.stride(2) != 1)):
@@ -709,7 +763,8 @@ class CudaKernels:
         out = torch.empty(T, H, R, dtype=q_latent.dtype, device=self.device)
         if (self.use_mma_latent_attention and q_latent.dtype == torch.bfloat16 and view.rows.is_contiguous() and scale > 0
                 and q_latent.stride(0) % 8 == 0 and q_latent.stride(1) % 8 == 0 and q_latent.data_ptr() % 16 == 0
-                and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(view.window or 0))):
+                and amplitude == 1.0
+                and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(window or 0))):
             # tensor cores; few blocks (decode): the keys are split over blocks and merged afterwards
             per_tile = int(self.lib.ttb_latent_attention_mma_tokens_per_tile(H))
             blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // (256 if R > 128 else 128))
@@ -731,14 +786,14 @@ class CudaKernels:
             if splits > 1 and merge:
                 self.launches += 1
             return out, partial_o, partial_ml, splits
-        self._check(self.lib.ttb_latent_attention_generic(
+        self._check(self.lib.ttb_latent_attention_generic_ext(
             self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
             self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
             ctypes.c_longlong(q_rot.stride(1) if q_rot is not None else 0), self._p(out), _dtype_code(q_latent.dtype),
             self._p(batch.positions), self._p(batch.seg_of_token), self._p(view.rows), self._p(view.block_table),
             view.block_table.shape[1], view.page_size, T, H, R, view.extra, ctypes.c_float(scale), self._p(sinks),
-            self._p(inv_freq), int(rotary_dim), int(view.window or 0), view.rows.shape[0], self._p(self.status),
-            self._stream()), "latent_attention")
+            self._p(inv_freq), int(rotary_dim), int(window or 0), view.rows.shape[0], self._p(self.status),
+            ctypes.c_float(amplitude), self._stream()), "latent_attention")
         return out, None, None, 1
 
     def gate_heads(self, out, gate):
@@ -780,6 +835,30 @@ class CudaKernels:
                                                   self._p(gate), self._ROUTER_SCORES[scores], self._stream()), "route_top")
         return choice, weight, gate
 
+    def route_corrected(self, x, w_router, correction, experts, top, scale, floor):
+        """Float32 router with a score per expert, s = sigmoid(W_r x): the `top` experts with the largest s + correction
+        are chosen (the lower index among equals), their weights are s / (sum of the chosen s + floor) * scale.
+        -> (int32 [T, top], float32 [T, top])."""
+        T, width = x.shape
+        if (w_router.dtype != torch.float32 or w_router.shape != (experts, width) or x.stride(1) != 1
+                or correction.dtype != torch.float32 or correction.shape != (experts,)):
+            raise KernelError("route_corrected: the router's matrix must be float32 [experts, width], the corrections float32 [experts]")
+        choice = torch.empty(T, top, dtype=torch.int32, device=self.device)
+        weight = torch.empty(T, top, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_route_top_corrected(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(w_router), T, width,
+                                                     experts, top, 0, self._p(choice), self._p(weight), None, 2,
+                                                     self._p(correction), ctypes.c_float(scale), ctypes.c_float(floor),
+                                                     self._stream()), "route_corrected")
+        return choice, weight
+
+    def _ones(self, count):
+        """`count` float32 ones on the device; made once and sliced."""
+        have = getattr(self, "_ones_buffer", None)
+        if have is None or have.numel() < count:
+            have = torch.ones(max(count, 1 << 16), dtype=torch.float32, device=self.device)
+            self._ones_buffer = have
+        return have[:count]
+
     def glu_clamped(self, gate_up, limit, alpha):
         rows, two = gate_up.shape
         out = torch.empty(rows, two // 2, dtype=gate_up.dtype, device=self.device)
@@ -804,6 +883,8 @@ class CudaKernels:
         pairs = T * top
         if x.dtype != w_gate_up.dtype or x.stride(1) != 1 or not w_gate_up.is_contiguous() or not w_down.is_contiguous():
             raise KernelError("routed_experts: operands must share a dtype and be contiguous")
+        if shared is not None and shared_gate is None:
+            shared_gate = self._ones(T)                    # a shared expert without a gate of its own
         if shared is not None and (shared_gate is None or not shared[0].is_contiguous() or not shared[1].is_contiguous()):
             raise KernelError("routed_experts: the shared expert needs contiguous weights and a gate per token")
         out = torch.empty(T, width, dtype=torch.float32, device=self.device)
@@ -919,13 +1000,13 @@ class CudaKernels:
                     "mean_rmsnorm_pair")
         return out
 
-    _ACTIVATIONS = {"silu": 0, "gelu_tanh": 1, "relu2": 2, "gelu_erf": 3}
+    _ACTIVATIONS = {"silu": 0, "gelu_tanh": 1, "relu2": 2, "gelu_erf": 3, "relu": 4}
 
     def glu_activation(self, gate_up, activation):
-        """act(gate) * up over [rows, gate | up] -> [rows, columns / 2]; activation "silu" or "gelu_tanh"."""
+        """act(gate) * up over [rows, gate | up] -> [rows, columns / 2]; activation "silu", "relu" or "gelu_tanh"."""
         rows, two = gate_up.shape
-        if gate_up.stride(1) != 1 or activation not in ("silu", "gelu_tanh"):
-            raise KernelError("glu_activation: the product must be contiguous along its columns; silu or gelu_tanh")
+        if gate_up.stride(1) != 1 or activation not in ("silu", "gelu_tanh", "relu"):
+            raise KernelError("glu_activation: the product must be contiguous along its columns; silu, relu or gelu_tanh")
         out = torch.empty(rows, two // 2, dtype=gate_up.dtype, device=self.device)
         self._check(self.lib.ttb_activation(self._p(gate_up), _dtype_code(gate_up.dtype), gate_up.stride(0), self._p(out),
                                             _dtype_code(out.dtype), rows, two // 2, self._ACTIVATIONS[activation],
@@ -1037,12 +1118,14 @@ class CudaKernels:
 
     # ------------------------------------------------------------------ attention with a sink, a cap, chunks
     def qk_norm_rope_write(self, qkv, batch, q_norm, k_norm, eps, inv_freq, rotary_dim, heads, kv_heads, dim, vdim, view,
-                           write_kv=True, whole=False, amplitude=1.0):
+                           write_kv=True, whole=False, amplitude=1.0, bias=None, q_temp=None):
         """In place on qkv [T, heads * dim | kv_heads * dim | kv_heads * vdim]: RMS norm per head of q and k (weights
         float32 [dim] or None), rotation of their first rotary_dim elements; keys and values go into their pages.
         whole: one RMS norm over all of a token's query elements and one over all of its key elements (weights float32
         [heads * dim] and [kv_heads * dim]); amplitude: what the rotation's cosines and sines are multiplied by."""
         tokens = qkv.shape[0]
+        if (bias is not None or q_temp is not None) and (whole or amplitude != 1.0):
+            raise KernelError("qk_norm_rope_write: biases and a query temperature come with the per-head norm and amplitude 1")
         if whole or amplitude != 1.0:
             if q_norm is not None and not whole:
                 raise KernelError("qk_norm_rope_write: a rotation amplitude comes with the norm over the whole projection, or none")
@@ -1069,23 +1152,31 @@ class CudaKernels:
         write = bool(write_kv and view is not None)
         if write and (view.keys.dtype != qkv.dtype or not view.keys.is_contiguous() or not view.values.is_contiguous()):
             raise KernelError("qk_norm_rope_write: cache pages must be contiguous and of the compute dtype")
-        self._check(self.lib.ttb_qk_norm_rope_write(
+        if bias is not None and (bias.dtype != torch.float32 or bias.shape != (qkv.shape[1],) or not bias.is_contiguous()):
+            raise KernelError("qk_norm_rope_write: the bias must be float32, one number per column of qkv")
+        coef, every = (float(q_temp[0]), int(q_temp[1])) if q_temp is not None else (0.0, 1)
+        self._check(self.lib.ttb_qk_norm_rope_write_ext(
             self._p(qkv), _dtype_code(qkv.dtype), qkv.stride(0), self._p(batch.positions), self._p(batch.seg_of_token),
             self._p(q_norm), self._p(k_norm), ctypes.c_float(eps), self._p(inv_freq), int(rotary_dim), tokens, heads, kv_heads,
             dim, vdim, self._p(view.keys if write else None), self._p(view.values if write else None),
             self._p(view.block_table if write else None), view.block_table.shape[1] if write else 0,
             view.page_size if write else 1, view.keys.shape[0] if write else 0, 1 if write else 0, self._p(self.status),
-            self._stream()), "qk_norm_rope_write")
+            self._p(bias), ctypes.c_float(coef), every, self._stream()), "qk_norm_rope_write")
 
-    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view):
+    def sink_attention(self, qkv, batch, heads, kv_heads, dim, vdim, scale, softcap, sinks, view, distance_bias=None):
         """Causal attention of the queries in qkv over the paged keys and values, with a cap on the scores, chunks or
-        a window (from the view) and a sink per head (float32 [heads] or None). -> [T, heads * vdim]."""
+        a window (from the view), a sink per head (float32 [heads] or None) and a bias by distance (float32
+        [heads, far + 1], added to the capped score; distances beyond `far` take the last column). -> [T, heads * vdim]."""
         tokens = qkv.shape[0]
         if view.keys.dtype != qkv.dtype:
             raise KernelError("sink_attention: cache pages and queries differ in dtype")
         out = torch.empty(tokens, heads * vdim, dtype=qkv.dtype, device=self.device)
+        if distance_bias is not None and (distance_bias.dtype != torch.float32 or distance_bias.dim() != 2
+                                          or distance_bias.shape[0] != heads or not distance_bias.is_contiguous()):
+            raise KernelError("sink_attention: the bias by distance must be float32 [heads, far + 1]")
         if (self.use_mma_attention and qkv.dtype == torch.bfloat16 and dim == vdim and qkv.stride(0) % 8 == 0
                 and qkv.data_ptr() % 16 == 0 and view.keys.is_contiguous() and view.values.is_contiguous()
+                and distance_bias is None
                 and self.lib.ttb_attention_mma_supports(heads, kv_heads, dim)):
             # keys and values of one size that the tensor-core kernel takes: 64-row tiles for prompt portions, the
             # decode shape for single tokens; key splits sized by what a query can see at most
@@ -1106,12 +1197,111 @@ class CudaKernels:
             if splits > 1:
                 self.launches += 1
             return out
-        self._check(self.lib.ttb_paged_attention_generic_ext(
+        self._check(self.lib.ttb_paged_attention_generic_bias(
             self._p(qkv), qkv.stride(0), self._p(out), _dtype_code(qkv.dtype), self._p(batch.positions),
             self._p(batch.seg_of_token), self._p(view.keys), self._p(view.values), self._p(view.block_table),
             view.block_table.shape[1], view.page_size, tokens, heads, kv_heads, dim, ctypes.c_float(scale),
             int(view.window or 0), view.keys.shape[0], self._p(self.status), vdim, ctypes.c_float(softcap or 0.0),
-            int(view.chunk or 0), self._p(sinks), self._stream()), "sink_attention")
+            int(view.chunk or 0), self._p(sinks), self._p(distance_bias),
+            distance_bias.shape[1] - 1 if distance_bias is not None else 0, self._stream()), "sink_attention")
+        return out
+
+    # ------------------------------------------------------------------ token shift, low-rank maps, matrix states
+    def token_shift(self, x, mu, batch, view):
+        """The mixes of every token with the token before it: out[t, s] = x[t] + (before[t] - x[t]) * mu[s], mu float32
+        [mixes, width]; before a segment's first token stands the request's kept input (view.tail), which the walk
+        refreshes afterwards. -> [T, mixes, width] in x's dtype."""
+        T, width = x.shape
+        if x.stride(1) != 1 or mu.dtype != torch.float32 or mu.shape[1] != width or not mu.is_contiguous():
+            raise KernelError("token_shift: contiguous columns, and float32 mixing weights [mixes, width]")
+        if view.tail.dtype != x.dtype or not view.tail.is_contiguous() or tuple(view.tail.shape[1:]) != (1, width):
+            raise KernelError("token_shift: one kept input of the model's width per request, of the compute dtype")
+        out = torch.empty(T, mu.shape[0], width, dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_token_shift(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(mu), mu.shape[0],
+                                             self._p(batch.seg_of_token), self._p(batch.cu_seqlens), self._p(view.slots),
+                                             self._p(view.tail), self._p(out), T, width, self._stream()), "token_shift")
+        return out
+
+    _LOWRANK_OUT = {"none": 0, "neg_exp": 1, "neg_rate_softplus": 2}
+
+    def lowrank_expand(self, x, w, bias, in_act, out_kind, rate=None):
+        """The second half of a low-rank map, in float32 arithmetic: f(act(x) W^T + bias). x float32 [T, rank] (a slice
+        of a wider product); W [N, rank] of the compute dtype; bias float32 [N] or None. in_act None or "tanh"; out_kind
+        "none", "neg_exp" (-exp(z)) or "neg_rate_softplus" (-rate[head] * softplus(z), rate float32 [heads], N = heads *
+        per_head). -> float32 [T, N]."""
+        T, rank = x.shape
+        N = w.shape[0]
+        if x.dtype != torch.float32 or x.stride(1) != 1 or w.shape[1] != rank or not w.is_contiguous():
+            raise KernelError("lowrank_expand: float32 input contiguous along its columns, and W [N, rank]")
+        if in_act not in (None, "tanh") or out_kind not in self._LOWRANK_OUT:
+            raise KernelError(f"lowrank_expand: in_act {in_act!r} or out_kind {out_kind!r} is not known")
+        out = torch.empty(T, N, dtype=torch.float32, device=self.device)
+        self._check(self.lib.ttb_lowrank_expand(
+            self._p(x), x.stride(0), self._p(w), _dtype_code(w.dtype), self._p(bias), self._p(rate),
+            rate.shape[0] if rate is not None else 1, 1 if in_act == "tanh" else 0, self._LOWRANK_OUT[out_kind], self._p(out),
+            T, N, rank, self._stream()), "lowrank_expand")
+        return out
+
+    def shifted_state(self, rkvg, log_decay, bonus, norm_w, eps, heads, dim, x, batch, view, write_state=True):
+        """rkvg [T, 4, heads * dim] (r, k, v and the gate before its silu; any token stride); log_decay float32 [T, heads * dim]
+        (ln w, never positive); per head o = (S + diag(bonus) k v^T)^T r, S = diag(w) S + k v^T on the float32 state of
+        view.state; then o / rms(o) per head, times norm_w, times silu(gate) -> [T, heads * dim]. Leaves the state and the
+        request's last input (x's last row of the segment) in the request's slot."""
+        T = rkvg.shape[0]
+        inner = heads * dim
+        if rkvg.shape[1:] != (4, inner) or rkvg.stride(2) != 1 or log_decay.dtype != torch.float32 or not log_decay.is_contiguous():
+            raise KernelError("shifted_state: rkvg [T, 4, heads * dim] contiguous along its last axis, float32 decays")
+        if (view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, dim, dim) or not view.state.is_contiguous()
+                or view.tail.dtype != x.dtype or not view.tail.is_contiguous() or x.dtype != rkvg.dtype or x.stride(1) != 1):
+            raise KernelError("shifted_state: the state must be float32 [slots, heads, dim, dim], the kept input of the compute dtype")
+        out = torch.empty(T, inner, dtype=rkvg.dtype, device=self.device)
+        self._check(self.lib.ttb_shifted_state(
+            self._p(rkvg), _dtype_code(rkvg.dtype), ctypes.c_longlong(rkvg.stride(0)), ctypes.c_longlong(rkvg.stride(1)),
+            self._p(log_decay), self._p(bonus), self._p(norm_w), ctypes.c_float(eps), self._p(x), ctypes.c_longlong(x.stride(0)),
+            x.shape[1], self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(out),
+            batch.num_segments, heads, dim, 1 if write_state else 0, self._stream()), "shifted_state")
+        return out
+
+    def short_conv_silu(self, x, conv_w, batch, view):
+        """silu of a causal convolution per channel without a bias: sum_j conv_w[:, j] * x[t - taps + 1 + j], reading the
+        request's kept inputs (view.tail) before the step's first token; they are refreshed by the mixer's walk. x [T, channels]."""
+        T, C = x.shape
+        taps = conv_w.shape[1]
+        if x.stride(1) != 1 or conv_w.dtype != torch.float32 or conv_w.shape[0] != C or not conv_w.is_contiguous():
+            raise KernelError("short_conv_silu: contiguous columns, float32 taps [channels, taps]")
+        if view.tail.dtype != x.dtype or not view.tail.is_contiguous() or view.tail.shape[2] != C:
+            raise KernelError("short_conv_silu: kept inputs of the compute dtype over the same channels")
+        zeros = getattr(self, "_conv_zero_bias", None)
+        if zeros is None or zeros.numel() < C:
+            zeros = torch.zeros(max(C, 1 << 14), dtype=torch.float32, device=self.device)
+            self._conv_zero_bias = zeros
+        u = torch.empty(T, C, dtype=x.dtype, device=self.device)
+        self._check(self.lib.ttb_conv_silu(self._p(x), _dtype_code(x.dtype), x.stride(0), self._p(conv_w), self._p(zeros),
+                                           self._p(batch.seg_of_token), self._p(batch.cu_seqlens), self._p(view.slots),
+                                           self._p(view.tail), self._p(u), T, C, taps, self._stream()), "short_conv_silu")
+        return u
+
+    def delta_rule(self, u, raw, beta, log_decay, gate, norm_w, eps, heads, kv_heads, dim, vdim, batch, view, write_state=True):
+        """u [T, q | k | v] behind the convolutions (q, k: kv_heads * dim; v: heads * vdim), raw their inputs; beta float32
+        logits [T, heads] (a slice); log_decay float32 [T, heads * dim] (ln g); gate float32 logits [T, heads * vdim]. Per head,
+        with q and k made unit vectors (q also times dim^-1/2): S = diag(g) S; d = sigmoid(beta) (v - S^T k); S += k d^T;
+        o = S^T q; then o / rms(o), times norm_w [vdim], times sigmoid(gate) -> [T, heads * vdim]. Leaves the state and the
+        convolutions' last inputs in the request's slot."""
+        T, C = u.shape
+        if C != 2 * kv_heads * dim + heads * vdim or raw.shape != u.shape or u.stride(1) != 1 or raw.stride(1) != 1 or raw.dtype != u.dtype:
+            raise KernelError("delta_rule: u and raw must be [T, 2 kv_heads dim + heads vdim], contiguous along their columns")
+        if (beta.dtype != torch.float32 or beta.shape != (T, heads) or beta.stride(1) != 1 or log_decay.dtype != torch.float32
+                or not log_decay.is_contiguous() or gate.dtype != torch.float32 or not gate.is_contiguous()):
+            raise KernelError("delta_rule: float32 beta logits, decays and gate logits")
+        if (view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, dim, vdim) or not view.state.is_contiguous()
+                or view.tail.dtype != u.dtype or not view.tail.is_contiguous() or view.tail.shape[2] != C):
+            raise KernelError("delta_rule: the state must be float32 [slots, heads, dim, vdim], the kept inputs of the compute dtype")
+        out = torch.empty(T, heads * vdim, dtype=u.dtype, device=self.device)
+        self._check(self.lib.ttb_delta_rule(
+            self._p(u), _dtype_code(u.dtype), ctypes.c_longlong(u.stride(0)), self._p(raw), ctypes.c_longlong(raw.stride(0)),
+            self._p(beta), beta.stride(0), self._p(log_decay), self._p(gate), self._p(norm_w), ctypes.c_float(eps),
+            self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(out),
+            batch.num_segments, heads, kv_heads, dim, vdim, view.taps, 1 if write_state else 0, self._stream()), "delta_rule")
         return out
 
     # ------------------------------------------------------------------ experts chosen from the best groups
