@@ -162,6 +162,8 @@ def blended_frequencies(rot, dtype=F):
 
 def rotate_neighbours(x, positions, rot):
     """x [T, ..., n]: elements 2i and 2i + 1 of the first rot.dims form a pair."""
+    if not rot or not rot.get("dims") or x.shape[-1] == 0:
+        return x
     dims = rot["dims"]
     freq, amp = blended_frequencies(rot, x.dtype)
     angle = positions.to(x.dtype)[:, None] * freq[None, :]
@@ -179,15 +181,15 @@ def latent_of(h, w, p, m, eps):
     R = m["kv_rank"]
     down = h @ w[p + "dkv"].T
     c = rms(down[:, :R], eps) * w[p + "dkv.norm"]
-    return c, rotate_neighbours(down[:, R:], torch.arange(h.shape[0]), m["rot"])
+    return c, rotate_neighbours(down[:, R:], torch.arange(h.shape[0]), m.get("rot"))
 
 
 def latent_attention(h, w, p, m, eps, cached):
     T = h.shape[0]
-    H, D, Rd, V = m["heads"], m["dim"], m["rot_dim"], m["vdim"]
+    H, D, Rd, V = m["heads"], m["dim"], m.get("rot_dim", 0), m["vdim"]
     c, k_rot = cached
     q = (h @ w[p + "q"].T).view(T, H, D + Rd)
-    q_plain, q_rot = q[..., :D], rotate_neighbours(q[..., D:], torch.arange(T), m["rot"])
+    q_plain, q_rot = q[..., :D], rotate_neighbours(q[..., D:], torch.arange(T), m.get("rot"))
     k_plain = (c @ w[p + "uk"].T).view(T, H, D)
     v = (c @ w[p + "uv"].T).view(T, H, V)
     size = m["mask"]["size"] if m.get("mask") else T + 1
