@@ -52,7 +52,7 @@ def main(argv=None) -> int:
     parser.add_argument("--skip-e2e", action="store_true", help="leave the end-to-end measurement out (for profiling)")
     parser.add_argument("--design", default=None,
                         help="instead of the default workload: prefill and decode throughput of a named random model of "
-                             "another design (bozavik-a, bozavik-b, pedazen-a, pedazen-b, sezanex-a, sezanex-b) beside the closest dense model at equal size, with "
+                             "another design (bozavik-a, bozavik-b, pedazen-a, pedazen-b, sezanex-a, sezanex-b, bufolorn-a, bufolorn-b) beside the closest dense model at equal size, with "
                              "the design's own kernels against their rooflines")
     parser.add_argument("--fill", default="prefill", choices=("prefill", "synthetic"),
                         help="how the cache gets its context before decoding: through the engine's own prefill, "

@@ -98,6 +98,38 @@ def sezanex_config(width, blocks, ssm_heads, ssm_vdim, state, ssm_groups, heads,
     return cfg
 
 
+def bufolorn_config(width, blocks, heads, kv_heads, head_dim, state_heads, state_dim, latent_heads, latent_dim, rot_dim, latent_vdim,
+                    kv_rank, window, delta_heads, delta_kv_heads, delta_dim, delta_vdim, experts, top, ff, shared_ff, dense_ff, vocab):
+    """`blocks` times four layers: softmax attention with a distance bias beside a token-shift state (dense feed-forward),
+    latent attention over a window, a delta rule with channel decays, and latent attention that reads the latent of the
+    layer two before it (corrected experts with a shared one in all three)."""
+    def side_by_side():
+        left = {"heads": heads, "kv_heads": kv_heads, "dim": head_dim, "vdim": head_dim, "scale": head_dim ** -0.5 * 4, "softcap": 30.0,
+                "bias_max": 1024, "bias_rows": 32, "q_temp": {"coef": 0.3, "every": 1024}}
+        return {"type": "parallel", "mixer": {"left": left, "right": {"heads": state_heads, "dim": state_dim, "decay_rank": 64},
+                                              "left_scale": 0.5, "right_scale": 0.5}}
+
+    def latent(kv_from=None):
+        m = {"heads": latent_heads, "dim": latent_dim, "rot_dim": rot_dim, "vdim": latent_vdim, "kv_rank": kv_rank,
+             "scale": (latent_dim + rot_dim) ** -0.5, "mask": {"size": window},
+             "rot": {"base": 10000.0, "dims": rot_dim, "scaling": {"factor": 4.0, "original": 4096, "fast": 32.0, "slow": 1.0}}}
+        if kv_from is not None:
+            m["kv_from"] = kv_from
+        return {"type": "latent_attention", "mixer": m}
+
+    def delta():
+        return {"type": "channel_delta", "mixer": {"heads": delta_heads, "kv_heads": delta_kv_heads, "dim": delta_dim, "vdim": delta_vdim,
+                                                   "conv": 4, "decay_rank": 64, "gate_rank": 64}}
+
+    moe = {"kind": "moe", "expert": {"ff": ff}, "router": {"experts": experts, "top": top, "scale": 1.0}, "shared": {"ff": shared_ff}}
+    layers = []
+    for b in range(blocks):
+        layers += [dict(side_by_side(), mlp={"kind": "dense", "ff": dense_ff}), dict(latent(), mlp=moe), dict(delta(), mlp=moe),
+                   dict(latent(kv_from=4 * b + 1), mlp=moe)]
+    return {"architecture": "Bufolorn", "vocab": vocab, "width": width, "residual_mult": 0.5, "norm": {"eps": 1e-5},
+            "embedding": {"scale": 1.0}, "layers": layers}
+
+
 def layer_runs(cfg: dict) -> int:
     """How many layers a token passes in a configuration with a `loop`, looped layers counted every time."""
     loop = cfg.get("loop")
@@ -109,7 +141,16 @@ def closest_llama(cfg: dict) -> dict:
     depth and vocabulary. For Bozavik: the same heads (head size = unrotated + rotated query elements), one KV
     head per four heads, and a feed-forward as wide as the experts a token uses plus the shared one. For Pedazen:
     as many layers as a token passes, the heads, KV heads and head size of its softmax attention, and a
-    feed-forward as wide as the experts a token uses. For Sezanex: the same with its windowed attention's heads."""
+    feed-forward as wide as the experts a token uses. For Sezanex: the same with its windowed attention's heads. For
+    Bufolorn: the heads of its softmax attention, and a feed-forward as wide as the experts a token uses plus the shared one."""
+    if cfg.get("architecture") == "Bufolorn":
+        a = next(l["mixer"]["left"] for l in cfg["layers"] if l["type"] == "parallel")
+        f = next(l["mlp"] for l in cfg["layers"] if l["mlp"] and l["mlp"]["kind"] == "moe")
+        inter = f["router"]["top"] * f["expert"]["ff"] + (f.get("shared") or {}).get("ff", 0)
+        return {"architectures": ["LlamaForCausalLM"], "hidden_size": cfg["width"], "num_hidden_layers": len(cfg["layers"]),
+                "num_attention_heads": a["heads"], "num_key_value_heads": a["kv_heads"], "head_dim": a["dim"],
+                "intermediate_size": inter, "vocab_size": cfg["vocab"], "rms_norm_eps": 1e-5,
+                "max_position_embeddings": 131072, "rope_theta": 500000.0, "tie_word_embeddings": False}
     if cfg.get("architecture") == "Sezanex":
         a = next(l["mixer"] for l in cfg["layers"] if l["type"] == "attention")
         f = next(l["mlp"] for l in cfg["layers"] if l["mlp"] and l["mlp"]["kind"] == "moe")
@@ -152,6 +193,13 @@ RANDOM_MODELS.update({
     "sezanex-tiny": sezanex_config(128, 1, 4, 32, 32, 2, 4, 2, 64, 64, 4, 2, 64, 256, 512, loop=(1, 4, 2)),
     "sezanex-a": sezanex_config(1024, 2, 32, 64, 128, 2, 16, 4, 64, 1024, 16, 4, 512, 2048, 32768, loop=(2, 4, 2)),
     "sezanex-b": sezanex_config(2048, 2, 64, 64, 128, 4, 16, 4, 128, 2048, 32, 4, 1024, 4096, 65536, loop=(2, 4, 2)),
+})
+
+
+RANDOM_MODELS.update({
+    "bufolorn-tiny": bufolorn_config(128, 1, 4, 2, 64, 2, 32, 4, 16, 16, 32, 64, 64, 4, 2, 32, 32, 4, 2, 64, 64, 256, 512),
+    "bufolorn-a": bufolorn_config(1024, 2, 16, 4, 64, 16, 64, 16, 32, 32, 64, 128, 1024, 16, 4, 64, 64, 16, 4, 512, 512, 2048, 32768),
+    "bufolorn-b": bufolorn_config(2048, 2, 16, 4, 128, 32, 64, 16, 64, 64, 128, 256, 2048, 16, 4, 128, 128, 32, 4, 1024, 1024, 4096, 65536),
 })
 
 

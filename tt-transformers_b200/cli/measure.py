@@ -559,6 +559,9 @@ _TIMED = {"Bozavik": ["add_layernorm", "latent_prepare", "heads_linear", "_laten
                       "glu_activation", "linear"],
           "Sezanex": ["add_dyntanh", "state_space", "qk_norm_rope_write", "sink_attention", "route_top", "input_weighted_experts",
                       "activation", "concat_cast", "linear"],
+          "Bufolorn": ["add_layernorm_sum", "token_shift", "heads_linear", "lowrank_expand", "shifted_state", "short_conv_silu",
+                       "delta_rule", "qk_norm_rope_write", "sink_attention", "latent_prepare", "_latent_attention", "latent_out",
+                       "gate_heads", "route_corrected", "routed_experts", "glu_activation", "linear"],
           "Llama": ["add_rmsnorm", "rope_kv_write", "fused_qkv_rope", "paged_attention", "linear_swiglu", "linear"]}
 
 
@@ -623,6 +626,48 @@ def _kernel_work(cfg: dict, tokens: int, contexts: List[int], new_per_request: i
                     used = min(experts, tokens * top)
                     add("plain_experts", 2.0 * tokens * 2 * top * ff * width, 2 * used * ff * 2 * width + tokens * width * (2 + 4))
                     add("route_grouped", 2.0 * tokens * experts * width, tokens * width * 2 + experts * width * 4)
+    elif cfg.get("architecture") == "Bufolorn":
+        width = cfg["width"]
+        segs = len(contexts)
+        for layer in cfg["layers"]:
+            m, f = layer["mixer"], layer["mlp"]
+            # the stream in and out, the layer's outputs in (two or three of them), h out
+            add("add_layernorm_sum", 0, tokens * width * (4 + 4 + 2 + (2 if layer["type"] == "parallel" else 0) + (3 if f else 0) + 2))
+            if layer["type"] == "parallel":
+                a, r = m["left"], m["right"]
+                H, G, D, V = a["heads"], a["kv_heads"], a["dim"], a["vdim"]
+                pairs = sum(n * new_per_request - new_per_request * (new_per_request - 1) / 2 for n in contexts)
+                add("sink_attention", 2.0 * H * pairs * (D + V), 2 * (sum(contexts) * G * (D + V) + tokens * H * (D + V)))
+                add("qk_norm_rope_write", 0, tokens * ((H + G) * D * 2 * 2 + G * (D + V) * 2 + G * V * 2))
+                SH, SD = r["heads"], r["dim"]
+                # per token and head: the read with the bonus (2 D^2) and the decayed update (2 D^2), however it is cut;
+                # r, k, v, the gate and the decays in, the output out, the state in and out
+                add("shifted_state", 4.0 * tokens * SH * SD * SD, tokens * SH * SD * (4 * 2 + 4 + 2) + 2 * segs * SH * SD * SD * 4)
+                work["shifted_state"]["fp32_flops"] = work["shifted_state"].get("fp32_flops", 0.0) + 4.0 * tokens * SH * SD * SD
+                add("token_shift", 0, tokens * width * (2 + 5 * 2))
+            elif layer["type"] == "channel_delta":
+                H, G, D, V = m["heads"], m["kv_heads"], m["dim"], m["vdim"]
+                C = 2 * G * D + H * V
+                # per token and head: decay (D V), S^T k (2 D V), the update (2 D V), S^T q (2 D V)
+                add("delta_rule", 7.0 * tokens * H * D * V, tokens * (C * 2 + H * D * 4 + H * V * 4 + H * V * 2) + 2 * segs * H * D * V * 4)
+                work["delta_rule"]["fp32_flops"] = work["delta_rule"].get("fp32_flops", 0.0) + 7.0 * tokens * H * D * V
+                add("short_conv_silu", 0, tokens * C * 2 * 2)
+            else:
+                dk = m["kv_rank"] + m.get("rot_dim", 0)
+                n = m["mask"]["size"] if m.get("mask") else 1 << 30
+                seen = sum(min(pos + 1, n) for ctx in contexts for pos in range(ctx - new_per_request, ctx))
+                keys_read = sum(min(ctx, n + new_per_request - 1) for ctx in contexts)
+                add("latent_attention", 2.0 * m["heads"] * seen * (dk + m["kv_rank"]),
+                    2 * (keys_read * dk + 2 * tokens * m["heads"] * m["kv_rank"]))
+                if m.get("kv_from") is None:
+                    add("latent_prepare", 0, tokens * (4 * dk + 2 * dk))
+            if f and f["kind"] == "moe":
+                top, ff, experts = f["router"]["top"], f["expert"]["ff"], f["router"]["experts"]
+                used = min(experts, tokens * top)
+                sff = (f.get("shared") or {}).get("ff", 0)          # the shared expert runs inside the same call
+                add("routed_experts", 2.0 * tokens * 3 * (top * ff + sff) * width,
+                    2 * (used * ff + sff) * 3 * width + tokens * width * (2 + 4))
+                add("route_corrected", 2.0 * tokens * experts * width, tokens * width * 2 + experts * width * 4)
     elif cfg.get("architecture") == "Sezanex":
         width = cfg["width"]
         loop = cfg.get("loop")
@@ -684,7 +729,7 @@ def _step_kernel_times(engine, family: str, entries_fn, reps: int = 3) -> Dict[s
 
 def run_design_comparison(name: str = "bozavik-a", *, prefill_tokens: int = PREFILL_TOKENS, batch: int = 8,
                           context: int = 4096, steps: int = 32, warmup: int = 4, device: str = "cuda:0") -> dict:
-    """Prefill and decode throughput of a named model of another design (Bozavik, Pedazen, Sezanex; random weights) and of the
+    """Prefill and decode throughput of a named model of another design (Bozavik, Pedazen, Sezanex, Bufolorn; random weights) and of the
     dense decoder closest to it at equal size, and, kernel by kernel, how far the design's own kernels are from their
     rooflines beside the like kernels of the dense model (eager steps, CUDA events around each kernel-table call)."""
     from ..engine.step import StepEntry
