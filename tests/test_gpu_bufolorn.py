@@ -163,6 +163,55 @@ def test_convolutions_and_delta_rule_against_their_twins(kernels, twin, dtype, H
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("H,G,D,V", [(2, 1, 64, 64), (3, 3, 24, 40), (2, 2, 128, 32), (1, 1, 5, 7)])
+def test_long_segments_run_as_parts(kernels, twin, dtype, H, G, D, V):
+    """Segments of several hundred tokens are cut into parts that run side by side and are folded in order: the same
+    outputs and end states as the walk token by token, beside short segments and single tokens, from states that are not zero."""
+    g = torch.Generator().manual_seed(H * D + V)
+    segs, slots = [(0, 300), (40, 1), (5, 700), (0, 64), (17, 257)], [3, 0, 4, 1, 2]
+    batch = _batch(segs, slots)
+    T = batch.num_tokens
+    assert batch.max_seg_len >= kernels.MATRIX_STATE_PARTS_FROM
+    # the delta rule
+    C, taps = 2 * G * D + H * V, 3
+    req = MatrixState(H, D, V, C, taps)
+    state = (torch.randn(6, H, D, V, generator=g) * 0.5).to(DEV)
+    tail = torch.randn(6, taps - 1, C, generator=g).to(DEV, dtype)
+    u = torch.randn(T, C, generator=g).to(DEV, dtype)
+    beta, gate = torch.randn(T, H, generator=g).to(DEV), torch.randn(T, H * V, generator=g).to(DEV)
+    log_decay = -(torch.rand(T, H * D, generator=g) * 0.3).to(DEV)
+    norm_w = (1 + 0.3 * torch.randn(V, generator=g)).to(DEV)
+    s_ref, s_got, t_ref, t_got = state.clone(), state.clone(), tail.clone(), tail.clone()
+    v_ref = req.view({"state": s_ref, "tail": t_ref}, slots=batch.seg_slot, slot_list=slots)
+    v_got = req.view({"state": s_got, "tail": t_got}, slots=batch.seg_slot, slot_list=slots)
+    ref = twin.delta_rule(u, u, beta, log_decay, gate, norm_w, 1e-5, H, G, D, V, batch, v_ref)
+    got = kernels.delta_rule(u, u, beta, log_decay, gate, norm_w, 1e-5, H, G, D, V, batch, v_got)
+    _close(got, ref, 2e-4 if dtype == torch.float32 else 2e-2)
+    _close(s_got, s_ref, 2e-4)
+    assert torch.equal(t_got, t_ref) and torch.equal(s_got[5], state[5])
+    kept = s_got.clone()
+    kernels.delta_rule(u, u, beta, log_decay, gate, norm_w, 1e-5, H, G, D, V, batch, v_got, write_state=False)
+    assert torch.equal(s_got, kept) and torch.equal(t_got, t_ref)
+    # the token-shift state
+    width = 40
+    req = MatrixState(H, D, D, width, 2)
+    state = (torch.randn(6, H, D, D, generator=g) * 0.5).to(DEV)
+    tail = torch.randn(6, 1, width, generator=g).to(DEV, dtype)
+    rkvg = (torch.randn(T, 4, H * D, generator=g) * D ** -0.25).to(DEV, dtype)
+    log_decay = -torch.exp(torch.randn(T, H * D, generator=g) * 1.5 - 2.5).to(DEV)
+    bonus, norm_w = torch.randn(H, D, generator=g).to(DEV), (1 + 0.3 * torch.randn(H * D, generator=g)).to(DEV)
+    x = torch.randn(T, width, generator=g).to(DEV, dtype)
+    s_ref, s_got, t_ref, t_got = state.clone(), state.clone(), tail.clone(), tail.clone()
+    v_ref = req.view({"state": s_ref, "tail": t_ref}, slots=batch.seg_slot, slot_list=slots)
+    v_got = req.view({"state": s_got, "tail": t_got}, slots=batch.seg_slot, slot_list=slots)
+    ref = twin.shifted_state(rkvg, log_decay, bonus, norm_w, 1e-5, H, D, x, batch, v_ref)
+    got = kernels.shifted_state(rkvg, log_decay, bonus, norm_w, 1e-5, H, D, x, batch, v_got)
+    _close(got, ref, 2e-4 if dtype == torch.float32 else 2e-2)
+    _close(s_got, s_ref, 2e-4)
+    assert torch.equal(t_got, t_ref) and torch.equal(s_got[5], state[5])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_tokens_and_keys_made_to_stand_out(kernels, dtype):
     check_the_matrix_states_keep_a_far_token(kernels, DEV, dtype)
     check_the_bonus_is_for_the_current_token_only(kernels, DEV, dtype)

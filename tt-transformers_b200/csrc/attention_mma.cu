@@ -68,10 +68,12 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
                      int heads, int kv_heads, float scale_log2, int window, int num_splits,
                      float* __restrict__ partial_o, float* __restrict__ partial_ml, int num_pages,
                      int* __restrict__ status, float softcap, float softcap_scale, int chunk_size,
-                     const float* __restrict__ sinks) {
+                     const float* __restrict__ sinks, const float* __restrict__ dist_bias, int far, float bias_mult) {
     // Options, all off at zero / null: softcap c: score = c * tanh(q.k * softcap_scale) with softcap_scale = scale / c
     // (scale_log2 is then log2(e) alone); chunk_size n: position p sees the keys from floor(p / n) * n on only;
-    // sinks: one more term 2^(sink_h * log2(e)) of every row's denominator, with no value (it joins in split 0).
+    // sinks: one more term 2^(sink_h * log2(e)) of every row's denominator, with no value (it joins in split 0);
+    // dist_bias [heads, far + 1]: dist_bias[h, min(p - key, far)] joins the (capped) score, as it is: bias_mult is 1
+    // with a cap and 1 / scale without one, where the scores stay unscaled until the exponent.
     constexpr int BM = 16 * WM;
     constexpr int THREADS = WM * WN * 32;
     constexpr int CHUNKS = HD / 8;              // 16-byte chunks per row
@@ -225,6 +227,25 @@ attention_mma_kernel(const __nv_bfloat16* __restrict__ qkv, int q_row_stride, __
                     for (int j = 0; j < 4; ++j) s[nb][j] = softcap * tanhf(s[nb][j] * softcap_scale);
             }
             const int last_key = key_base + WARP_KEYS - 1;
+            if (dist_bias != nullptr) {
+                const float* b0 = dist_bias + (size_t)(g * rep + r0 % rep) * (far + 1);
+                const float* b1 = dist_bias + (size_t)(g * rep + r1 % rep) * (far + 1);
+                if (warp_qpos_min - last_key >= far) {          // every key of the part lies beyond `far` for every row
+                    const float c0 = b0[far] * bias_mult, c1 = b1[far] * bias_mult;
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb) { s[nb][0] += c0; s[nb][1] += c0; s[nb][2] += c1; s[nb][3] += c1; }
+                } else {
+#pragma unroll
+                    for (int nb = 0; nb < NB; ++nb) {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            const int key = key_base + nb * 8 + ((lane & 3) << 1) + (j & 1);
+                            const int d = ((j < 2) ? qpos0 : qpos1) - key;
+                            s[nb][j] += ((j < 2) ? b0 : b1)[d < 0 ? 0 : (d > far ? far : d)] * bias_mult;
+                        }
+                    }
+                }
+            }
             const bool cut = last_key > warp_qpos_min || last_key >= k_end ||
                              (window > 0 && key_base <= warp_qpos_max - window) ||
                              (chunk_size > 0 && key_base < warp_qpos_max / chunk_size * chunk_size);
@@ -457,7 +478,7 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
                             int page_size, const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
                             int heads, int kv_heads, float scale, int window, int num_splits, float* partial_o,
                             float* partial_ml, int num_pages, int* status, float softcap, int chunk_size, const float* sinks,
-                            cudaStream_t stream) {
+                            cudaStream_t stream, const float* dist_bias, int far) {
     constexpr int BM = 16 * WM;
     const size_t stage_bytes = (size_t)BM * HD * 2 + 2 * (size_t)STAGES * AM_BN * HD * 2 + AM_TABLE_CACHE * sizeof(int);
     const size_t merge_bytes = (size_t)BM * HD * 2 + (size_t)WN * 16 * (HD + 2) * sizeof(float);
@@ -479,7 +500,7 @@ static int launch_attention(const void* qkv, int q_row_stride, void* out, const 
         (const __nv_bfloat16*)qkv, q_row_stride, (__nv_bfloat16*)out, cu_seqlens, seg_pos0,
         (const __nv_bfloat16*)key_pages, (const __nv_bfloat16*)value_pages, block_table, table_width, page_size,
         page_shift, qtile_seg, qtile_tok0, heads, kv_heads, scale_log2, window, num_splits, partial_o, partial_ml,
-        num_pages, status, softcap, softcap_scale, chunk_size, sinks);
+        num_pages, status, softcap, softcap_scale, chunk_size, sinks, dist_bias, far, softcap > 0.f ? 1.f : 1.f / scale);
     int launch = ttb_launch_status();
     if (launch != TTB_OK || num_splits == 1) return launch;
     const int rows = tokens * heads;
@@ -532,9 +553,10 @@ static int paged_attention_mma_impl(const void* qkv, int q_row_stride, void* out
                                     const int* qtile_tok0, int n_qtiles, int tokens, int heads, int kv_heads,
                                     int head_dim, float scale, int window, int decode_shape, int num_splits,
                                     float* partial_o, float* partial_ml, int num_pages, int* status,
-                                    cudaStream_t stream, float softcap = 0.f, int chunk_size = 0, const float* sinks = nullptr) {
+                                    cudaStream_t stream, float softcap = 0.f, int chunk_size = 0, const float* sinks = nullptr,
+                                    const float* dist_bias = nullptr, int far = 0) {
     if (n_qtiles == 0 || tokens == 0) return TTB_OK;
-    if (softcap < 0.f || chunk_size < 0) return TTB_ERR_ARGUMENT;
+    if (softcap < 0.f || chunk_size < 0 || (dist_bias && (far < 0 || !(scale > 0.f)))) return TTB_ERR_ARGUMENT;
     if (!qkv || !out || !cu_seqlens || !seg_pos0 || !key_pages || !value_pages || !block_table) return TTB_ERR_ARGUMENT;
     if (!ttb_attention_mma_supports(heads, kv_heads, head_dim)) return TTB_ERR_UNSUPPORTED;
     if (num_splits < 1 || num_splits > 65535 || kv_heads > 65535) return TTB_ERR_UNSUPPORTED;
@@ -544,7 +566,7 @@ static int paged_attention_mma_impl(const void* qkv, int q_row_stride, void* out
     if (decode_shape && heads / kv_heads > 16) return TTB_ERR_UNSUPPORTED;
 #define AM_ARGS qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table, table_width, page_size, \
                 qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads, scale, window, num_splits, partial_o, partial_ml, \
-                num_pages, status, softcap, chunk_size, sinks, stream
+                num_pages, status, softcap, chunk_size, sinks, stream, dist_bias, far
     if (head_dim == 64) return decode_shape ? launch_attention<64, 1, 4, 4>(AM_ARGS) : launch_attention<64, 4, 1, 3>(AM_ARGS);
     return decode_shape ? launch_attention<128, 1, 4, 3>(AM_ARGS) : launch_attention<128, 4, 1, 2>(AM_ARGS);
 #undef AM_ARGS
@@ -589,6 +611,21 @@ TTB_EXPORT int ttb_paged_attention_mma_ext(const void* qkv, int q_row_stride, vo
                                     table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
                                     head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
                                     num_pages, status, stream, softcap, chunk_size, sinks);
+}
+
+// The same with a bias by distance, float32 [heads, far + 1] (null: none): dist_bias[h, min(p - key, far)] joins the capped score.
+TTB_EXPORT int ttb_paged_attention_mma_bias(const void* qkv, int q_row_stride, void* out, const int* cu_seqlens,
+                                            const int* seg_pos0, const void* key_pages, const void* value_pages,
+                                            const int* block_table, int table_width, int page_size,
+                                            const int* qtile_seg, const int* qtile_tok0, int n_qtiles, int tokens,
+                                            int heads, int kv_heads, int head_dim, float scale, int window,
+                                            int decode_shape, int num_splits, float* partial_o, float* partial_ml,
+                                            int num_pages, int* status, float softcap, int chunk_size, const float* sinks,
+                                            const float* dist_bias, int far, cudaStream_t stream) {
+    return paged_attention_mma_impl(qkv, q_row_stride, out, cu_seqlens, seg_pos0, key_pages, value_pages, block_table,
+                                    table_width, page_size, qtile_seg, qtile_tok0, n_qtiles, tokens, heads, kv_heads,
+                                    head_dim, scale, window, decode_shape, num_splits, partial_o, partial_ml,
+                                    num_pages, status, stream, softcap, chunk_size, sinks, dist_bias, far);
 }
 
 // ---------------------------------------------------------------------------------------------

@@ -74,6 +74,8 @@ struct LatentMmaArgs {
     int latent, extra, rotary_dim;
     float scale_log2; const float* sinks; const float* inv_freq;
     int splits; float* partial_o; float* partial_ml; int* status;
+    int window;      // 0: every earlier key; w: a query at position p sees the keys above p - w
+    float amplitude; // what the rotation's cosines and sines are multiplied by
     int paired;      // a block takes two query tiles (one from each end of the segment) or one
     int stages;      // key tiles in shared memory at a time: 2 (the next one is fetched under the products) or 1
 };
@@ -119,7 +121,7 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
                         float sn, cs;
                         sincosf((float)(pos0 + r / nh) * a.inv_freq[f], &sn, &cs);
                         const float other = __bfloat162float(rsrc[d < half ? d + half : d - half]);
-                        v = d < half ? v * cs - other * sn : v * cs + other * sn;
+                        v = (d < half ? v * cs - other * sn : v * cs + other * sn) * a.amplitude;
                     }
                 }
                 Qs[r * ldq + a.latent + d] = __float2bfloat16_rn(v);
@@ -129,9 +131,10 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
 
     // ---- which key tiles are this block's
     const int last_key = pos0 + ntok - 1;
-    const int nk = last_key / LM_KEYS + 1;
+    const int first_key = (a.window > 0 && pos0 - a.window + 1 > 0) ? pos0 - a.window + 1 : 0;   // what the tile's first token sees
+    const int kt_first = first_key / LM_KEYS, nk = last_key / LM_KEYS + 1 - kt_first;
     const int per = (nk + a.splits - 1) / a.splits;
-    const int kt_begin = split * per, kt_end = min(nk, kt_begin + per);
+    const int kt_begin = kt_first + split * per, kt_end = min(kt_first + nk, kt_begin + per);
 
     const int r0 = warp * 16 + g, r1 = r0 + 8;
     const int row_pos0 = r0 < valid_rows ? pos0 + r0 / nh : -1;      // -1: no key is visible, the row is idle
@@ -154,7 +157,7 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
         const int key = kt * LM_KEYS + frow;
         const __nv_bfloat16* src = a.rows;
         int bytes = 0;
-        if (key <= last_key) {
+        if (key <= last_key && key >= first_key) {         // pages behind the window may be somebody else's by now
             const int page = table[key / a.page_size];
             if ((unsigned)page < (unsigned)a.num_pages) {
                 src = a.rows + ((size_t)page * a.page_size + key % a.page_size) * dk + fhalf_off;
@@ -177,6 +180,7 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
     const uint32_t rows16 = (uint32_t)(16 * ldq * 2);
     // rows of this warp that see every key of a tile need no mask for it
     const int warp_min_pos = (warp * 16 + 16 <= valid_rows) ? pos0 + (warp * 16) / nh : -1;
+    const int warp_max_pos = pos0 + (min(warp * 16 + 15, valid_rows - 1)) / nh;
     if (kt_begin < kt_end) fetch(kt_begin, ks_u32);
     for (int kt = kt_begin; kt < kt_end; ++kt) {
         const uint32_t kt_u32 = ks_u32 + ((kt - kt_begin) & 1) * second;
@@ -211,6 +215,16 @@ __device__ __forceinline__ void latent_attention_tile(const LatentMmaArgs& a, in
                 if (key + 1 > row_pos0) s[j][1] = -INFINITY;
                 if (key > row_pos1) s[j][2] = -INFINITY;
                 if (key + 1 > row_pos1) s[j][3] = -INFINITY;
+            }
+        }
+        if (a.window > 0 && kt * LM_KEYS <= warp_max_pos - a.window) {       // keys that a row's window has passed
+#pragma unroll
+            for (int j = 0; j < LM_KEYS / 8; ++j) {
+                const int key = kt * LM_KEYS + 8 * j + 2 * t4;
+                if (key <= row_pos0 - a.window) s[j][0] = -INFINITY;
+                if (key + 1 <= row_pos0 - a.window) s[j][1] = -INFINITY;
+                if (key <= row_pos1 - a.window) s[j][2] = -INFINITY;
+                if (key + 1 <= row_pos1 - a.window) s[j][3] = -INFINITY;
             }
         }
         float mx0 = -INFINITY, mx1 = -INFINITY;
@@ -365,7 +379,7 @@ static int tc_like_sm_count() {
 }
 
 TTB_EXPORT int ttb_latent_attention_mma_supports(int latent, int extra, int rotary_dim, int window) {
-    if (latent < 16 || (latent & 15) || (extra & 15) || extra < 0 || window > 0) return 0;
+    if (latent < 16 || (latent & 15) || (extra & 15) || extra < 0 || window < 0) return 0;
     if (rotary_dim > extra || (rotary_dim & 1)) return 0;
     const size_t smem = (size_t)(LM_ROWS + LM_KEYS) * (latent + extra + 8) * 2;
     return smem <= 220 * 1024;
@@ -380,16 +394,16 @@ TTB_EXPORT int ttb_latent_attention_mma_tokens_per_tile(int heads) {
 // q_lat [tokens, heads, latent] and q_rot [tokens, heads, extra] with element strides (token, head, 1), 16-byte
 // aligned rows; out [tokens, heads, latent] contiguous; rows [num_pages, page_size, latent + extra]. With
 // splits > 1: partial_o tokens * heads * splits * latent floats, partial_ml tokens * heads * splits * 2 floats.
-TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t, long long ql_stride_h, const void* q_rot,
+TTB_EXPORT int ttb_latent_attention_mma_ext(const void* q_lat, long long ql_stride_t, long long ql_stride_h, const void* q_rot,
                                         long long qr_stride_t, long long qr_stride_h, void* out, const int* cu_seqlens,
                                         const int* seg_pos0, const void* rows, const int* block_table, int table_width,
                                         int page_size, int num_pages, int segments, int max_seg_len, int tokens, int heads,
                                         int latent, int extra, float scale, const float* sinks, const float* inv_freq,
                                         int rotary_dim, int splits, float* partial_o, float* partial_ml, int merge,
-                                        int* status, cudaStream_t stream) {
+                                        int* status, int window, float amplitude, cudaStream_t stream) {
     if (tokens == 0 || segments == 0) return TTB_OK;
     if (!q_lat || !out || !cu_seqlens || !seg_pos0 || !rows || !block_table || !status) return TTB_ERR_ARGUMENT;
-    if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, 0) || !(scale > 0.f)) return TTB_ERR_UNSUPPORTED;
+    if (!ttb_latent_attention_mma_supports(latent, extra, rotary_dim, window) || !(scale > 0.f)) return TTB_ERR_UNSUPPORTED;
     if (extra > 0 && (!q_rot || (rotary_dim > 0 && !inv_freq))) return TTB_ERR_ARGUMENT;
     if ((ql_stride_t & 7) || (ql_stride_h & 7) || !aligned16(q_lat) || !aligned16(rows) || !aligned16(out)) return TTB_ERR_ARGUMENT;
     if (splits < 1 || splits > 64 || (splits > 1 && (!partial_o || !partial_ml))) return TTB_ERR_ARGUMENT;
@@ -408,6 +422,7 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     a.latent = latent; a.extra = extra; a.rotary_dim = rotary_dim;
     a.scale_log2 = scale * 1.4426950408889634f; a.sinks = sinks; a.inv_freq = inv_freq;
     a.splits = splits; a.partial_o = partial_o; a.partial_ml = partial_ml; a.status = status;
+    a.window = window; a.amplitude = amplitude;
     // with blocks in plenty a block takes a long tile and its short partner (even work); else one tile, longest first
     a.paired = (long long)segments * a.tiles_per_seg >= 16LL * tc_like_sm_count();
     const long long blocks_x = (long long)segments * (a.paired ? (a.tiles_per_seg + 1) / 2 : a.tiles_per_seg);
@@ -431,4 +446,17 @@ TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t
     ttb_launch(latent_attention_merge_kernel, tokens * heads, 128, 0, stream, (const float*)partial_o,
                (const float*)partial_ml, (__nv_bfloat16*)out, splits, latent);
     return ttb_launch_status();
+}
+
+TTB_EXPORT int ttb_latent_attention_mma(const void* q_lat, long long ql_stride_t, long long ql_stride_h, const void* q_rot,
+                                        long long qr_stride_t, long long qr_stride_h, void* out, const int* cu_seqlens,
+                                        const int* seg_pos0, const void* rows, const int* block_table, int table_width,
+                                        int page_size, int num_pages, int segments, int max_seg_len, int tokens, int heads,
+                                        int latent, int extra, float scale, const float* sinks, const float* inv_freq,
+                                        int rotary_dim, int splits, float* partial_o, float* partial_ml, int merge,
+                                        int* status, cudaStream_t stream) {
+    return ttb_latent_attention_mma_ext(q_lat, ql_stride_t, ql_stride_h, q_rot, qr_stride_t, qr_stride_h, out, cu_seqlens, seg_pos0,
+                                        rows, block_table, table_width, page_size, num_pages, segments, max_seg_len, tokens, heads,
+                                        latent, extra, scale, sinks, inv_freq, rotary_dim, splits, partial_o, partial_ml, merge,
+                                        status, 0, 1.f, stream);
 }

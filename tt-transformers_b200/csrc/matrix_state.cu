@@ -14,6 +14,14 @@
 // in tiles of MS_TILE through shared memory; a tile's outputs are normed and written by the whole block. Every state
 // element is updated by one thread in the order of the tokens, so a request's result does not depend on how it was cut
 // into steps or what else the batch holds. Decays arrive as logarithms (float32, never positive) and are exponentiated here.
+//
+// Long segments run as parts of `part_len` tokens side by side, in three launches. Both recurrences are linear in the
+// state, S_end = M S_start + E, column by column: (1) every part walks from a zero state to its E, and, for the delta
+// rule, D more columns that start as the identity and are fed zeros as values, which end as M (the token-shift state's M
+// is diagonal: the product of the part's decays, kept as the sum of their logarithms); (2) a block per head folds the
+// parts in order, S_(p+1) = M_p S_p + E_p, from the request's state, leaves every part's start state and the
+// request's new state; (3) every part walks again from its start state and writes its outputs. Parts start at multiples
+// of part_len from the first token that a step brings for a request.
 #include "common.cuh"
 
 #define MS_TILE 16
@@ -161,7 +169,14 @@ struct MsArgs {
     int taps;
     void* out;                   // [T, heads * V]
     int heads, kv_heads, D, V, R, write;
+    int mode;                    // 0: the whole segment; 1: a part from zero to its end state (and transition); 2: a part from its start state
+    int parts, part_len;
+    float* part_end;             // [segments, heads, parts, D, V (+ D for the delta rule)]
+    float* part_start;           // [segments, heads, parts, D, V]
+    float* part_log;             // shifted_state: [segments, heads, parts, D], the sums of the parts' log decays
 };
+
+template <bool DELTA> static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream);
 
 template <int DR, bool DELTA>
 __global__ void __launch_bounds__(DR == 64 ? MS_MAX_THREADS : 512)
@@ -173,30 +188,42 @@ matrix_state_walk_kernel(const MsArgs p) {
     float* sw = sb + MS_TILE * D;              // [TILE, D]  decay
     float* sc = sw + MS_TILE * D;              // [TILE, V]  v
     float* so = sc + MS_TILE * V;              // [TILE, V]  outputs
-    float* part = so + MS_TILE * V;            // [2, R, V]
-    float* sbeta = part + 2 * R * V;           // [TILE]
+    float* part_sums = so + MS_TILE * V;       // [2, R, V (+ D)]
+    float* sbeta = part_sums + 2 * R * (V + (DELTA ? D : 0));   // [TILE]
     float* sbonus = sbeta + MS_TILE;           // [D]
     float* sscale = sbonus + D;                // [TILE, 2]: unit-norm factors of q and k (delta), then the outputs' norm
     pdl_wait();
     pdl_launch_dependents();
-    const int seg = blockIdx.x, head = blockIdx.y;
+    const int seg = blockIdx.x, head = blockIdx.y, part = blockIdx.z;
     const int kvh = DELTA ? head / (p.heads / p.kv_heads) : head;
     const int tid = threadIdx.x, nthreads = blockDim.x;
-    const int col = tid % V, grp = tid / V;
+    const int VA = (DELTA && p.mode == 1) ? V + D : V;         // columns walked: the transition's ride along in mode 1
+    const int col = tid % VA, grp = tid / VA;
     const bool active = grp < R;
     const int row0 = grp * DR;
     const int start = p.cu_seqlens[seg], len = p.cu_seqlens[seg + 1] - start;
+    const int t_begin = p.mode == 0 ? 0 : part * p.part_len;
+    const int t_end = p.mode == 0 ? len : min(len, t_begin + p.part_len);
+    if (p.mode != 0 && t_begin >= t_end) return;
     const int slot = p.slots[seg];
+    const size_t part_index = ((size_t)seg * p.heads + head) * p.parts + part;
     float* state = p.state + ((size_t)slot * p.heads + head) * D * V;
     float S[DR];
 #pragma unroll
-    for (int i = 0; i < DR; ++i) S[i] = (active && row0 + i < D) ? state[(size_t)(row0 + i) * V + col] : 0.f;
+    for (int i = 0; i < DR; ++i) {
+        S[i] = 0.f;
+        if (active && row0 + i < D) {
+            if (p.mode == 0) S[i] = state[(size_t)(row0 + i) * V + col];
+            else if (p.mode == 2) S[i] = p.part_start[part_index * D * V + (size_t)(row0 + i) * V + col];
+            else if (col >= V) S[i] = (row0 + i == col - V) ? 1.f : 0.f;
+        }
+    }
     if (!DELTA)
         for (int d = tid; d < D; d += nthreads) sbonus[d] = p.bonus[(size_t)head * D + d];
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
     int turn = 0;
-    for (int t0 = 0; t0 < len; t0 += MS_TILE) {
-        const int nt = min(MS_TILE, len - t0);
+    for (int t0 = t_begin; t0 < t_end; t0 += MS_TILE) {
+        const int nt = min(MS_TILE, t_end - t0);
         __syncthreads();                       // the tile before is written out
         for (int i = tid; i < nt * D; i += nthreads) {
             const int tt = i / D, d = i - tt * D;
@@ -231,37 +258,53 @@ matrix_state_walk_kernel(const MsArgs p) {
             const float* a = sa + tt * D + row0;
             const float* b = sb + tt * D + row0;
             const float* w = sw + tt * D + row0;
-            float* mine = part + (size_t)turn * R * V;
+            float* mine = part_sums + (size_t)turn * R * VA;
             if (DELTA) {
                 float s = 0.f;
                 if (active) {
 #pragma unroll
                     for (int i = 0; i < DR; ++i)
                         if (row0 + i < D) { S[i] *= w[i]; s = fmaf(S[i], b[i], s); }
-                    mine[grp * V + col] = s;
+                    mine[grp * VA + col] = s;
                 }
                 __syncthreads();
                 float got = 0.f;
-                for (int g = 0; g < R; ++g) got += mine[g * V + col];
-                const float d = sbeta[tt] * (sc[tt * V + col] - got);
+                for (int g = 0; g < R; ++g) got += mine[g * VA + col];
+                const float d = sbeta[tt] * ((col < V ? sc[tt * V + col] : 0.f) - got);
                 turn ^= 1;
-                mine = part + (size_t)turn * R * V;
-                s = 0.f;
-                if (active) {
+                mine = part_sums + (size_t)turn * R * VA;
+                if (p.mode == 1) {                  // end states only: nobody reads this token's output
+                    if (active) {
 #pragma unroll
-                    for (int i = 0; i < DR; ++i)
-                        if (row0 + i < D) { S[i] = fmaf(b[i], d, S[i]); s = fmaf(S[i], a[i], s); }
-                    mine[grp * V + col] = s;
+                        for (int i = 0; i < DR; ++i)
+                            if (row0 + i < D) S[i] = fmaf(b[i], d, S[i]);
+                    }
+                } else {
+                    s = 0.f;
+                    if (active) {
+#pragma unroll
+                        for (int i = 0; i < DR; ++i)
+                            if (row0 + i < D) { S[i] = fmaf(b[i], d, S[i]); s = fmaf(S[i], a[i], s); }
+                        mine[grp * VA + col] = s;
+                    }
+                    __syncthreads();
+                    if (grp == 0) {
+                        float o = 0.f;
+                        for (int g = 0; g < R; ++g) o += mine[g * VA + col];
+                        so[tt * V + col] = o;
+                    }
+                    turn ^= 1;
                 }
-                __syncthreads();
-                if (grp == 0) {
-                    float o = 0.f;
-                    for (int g = 0; g < R; ++g) o += mine[g * V + col];
-                    so[tt * V + col] = o;
-                }
-                turn ^= 1;
             } else {
                 const float vc = sc[tt * V + col];
+                if (p.mode == 1) {                  // end states only
+                    if (active) {
+#pragma unroll
+                        for (int i = 0; i < DR; ++i)
+                            if (row0 + i < D) S[i] = fmaf(w[i], S[i], b[i] * vc);
+                    }
+                    continue;
+                }
                 float s = 0.f;
                 if (active) {
 #pragma unroll
@@ -283,6 +326,7 @@ matrix_state_walk_kernel(const MsArgs p) {
                 turn ^= 1;
             }
         }
+        if (p.mode == 1) continue;
         __syncthreads();
         // the tile's outputs: per head o / rms(o), a weight, the gate
         for (int tt = warp; tt < nt; tt += nwarps) {
@@ -301,10 +345,25 @@ matrix_state_walk_kernel(const MsArgs p) {
             ms_store(p.out, p.dtype, t * ((size_t)p.heads * V) + (size_t)head * V + c, so[i] * sscale[tt] * weight * gated);
         }
     }
-    if (!p.write || len == 0) return;
+    if (p.mode == 1) {                              // the part's end state from zero, the transition beside it
 #pragma unroll
-    for (int i = 0; i < DR; ++i)
-        if (active && row0 + i < D) state[(size_t)(row0 + i) * V + col] = S[i];
+        for (int i = 0; i < DR; ++i)
+            if (active && row0 + i < D) p.part_end[part_index * D * VA + (size_t)(row0 + i) * VA + col] = S[i];
+        if (!DELTA)
+            for (int d = tid; d < D; d += nthreads) {
+                float sum = 0.f;
+                for (int t = t_begin; t < t_end; ++t) sum += p.log_decay[(size_t)(start + t) * ((size_t)p.heads * D) + (size_t)head * D + d];
+                p.part_log[part_index * D + d] = sum;
+            }
+        return;
+    }
+    if (!p.write || len == 0) return;
+    if (p.mode == 2 && part != (len - 1) / p.part_len) return;      // the last part refreshes the kept inputs
+    if (p.mode == 0) {
+#pragma unroll
+        for (int i = 0; i < DR; ++i)
+            if (active && row0 + i < D) state[(size_t)(row0 + i) * V + col] = S[i];
+    }
     if (!DELTA) {
         // the kept input becomes the segment's last token; the heads share the columns between them
         const int c0 = (int)((long long)p.width * head / p.heads), c1 = (int)((long long)p.width * (head + 1) / p.heads);
@@ -335,21 +394,96 @@ matrix_state_walk_kernel(const MsArgs p) {
     }
 }
 
+// The parts folded in order: S_0 = the request's state; S_(p+1) = M_p S_p + E_p. A block per (segment, head); the state
+// in shared memory, twice for the delta rule (the new one is a product with the old one). Leaves every part's start state
+// in part_start and, with `write`, the state behind the last part in the request's slot.
+template <bool DELTA>
+__global__ void __launch_bounds__(256)
+matrix_state_fold_kernel(const MsArgs p) {
+    extern __shared__ __align__(16) float fold_smem[];
+    const int D = p.D, V = p.V, n = D * V;
+    float* cur = fold_smem;
+    float* next = fold_smem + n;                   // delta rule only
+    pdl_wait();
+    pdl_launch_dependents();
+    const int seg = blockIdx.x, head = blockIdx.y, tid = threadIdx.x;
+    const int len = p.cu_seqlens[seg + 1] - p.cu_seqlens[seg];
+    if (len == 0) return;
+    const int nparts = (len + p.part_len - 1) / p.part_len;
+    float* state = p.state + ((size_t)p.slots[seg] * p.heads + head) * n;
+    for (int i = tid; i < n; i += blockDim.x) cur[i] = state[i];
+    __syncthreads();
+    for (int part = 0; part < nparts; ++part) {
+        const size_t index = ((size_t)seg * p.heads + head) * p.parts + part;
+        float* begin = p.part_start + index * n;
+        for (int i = tid; i < n; i += blockDim.x) begin[i] = cur[i];
+        if (DELTA) {
+            const int VA = V + D;
+            const float* end = p.part_end + index * D * VA;           // row r: [E (V) | M (D)]
+            for (int i = tid; i < n; i += blockDim.x) {
+                const int r = i / V, c = i - r * V;
+                const float* row = end + (size_t)r * VA;
+                float acc = row[c];
+                for (int j = 0; j < D; ++j) acc = fmaf(row[V + j], cur[j * V + c], acc);
+                next[i] = acc;
+            }
+            __syncthreads();
+            float* t = cur; cur = next; next = t;
+        } else {
+            const float* end = p.part_end + index * n;
+            const float* logs = p.part_log + index * D;
+            for (int i = tid; i < n; i += blockDim.x) cur[i] = fmaf(expf(logs[i / V]), cur[i], end[i]);
+            __syncthreads();
+        }
+    }
+    if (p.write)
+        for (int i = tid; i < n; i += blockDim.x) state[i] = cur[i];
+}
+
 template <bool DELTA>
 static int ms_launch(MsArgs& p, int segments, cudaStream_t stream) {
     const int D = p.D, V = p.V;
     if (D < 1 || V < 1 || V > MS_MAX_THREADS || p.heads < 1 || p.heads > 65535) return TTB_ERR_UNSUPPORTED;
+    if (p.parts > 1) {
+        if (!p.part_end || !p.part_start || (!DELTA && !p.part_log) || p.part_len < 1 || p.parts > 65535) return TTB_ERR_ARGUMENT;
+        const size_t fold_smem = (size_t)(DELTA ? 2 : 1) * D * V * sizeof(float);
+        if (fold_smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+        MsArgs ends = p;
+        ends.mode = 1;
+        int rc = ms_launch_mode<DELTA>(ends, segments, stream);
+        if (rc != TTB_OK) return rc;
+        static TtbOncePerDevice once;
+        if (fold_smem > 48 * 1024 && once.pending()) {
+            cudaFuncSetAttribute(matrix_state_fold_kernel<DELTA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            once.mark();
+        }
+        ttb_launch(matrix_state_fold_kernel<DELTA>, dim3(segments, p.heads), 256, fold_smem, stream, p);
+        rc = ttb_launch_status();
+        if (rc != TTB_OK) return rc;
+        p.mode = 2;
+        return ms_launch_mode<DELTA>(p, segments, stream);
+    }
+    p.mode = 0;
+    p.parts = 1;
+    return ms_launch_mode<DELTA>(p, segments, stream);
+}
+
+template <bool DELTA>
+static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream) {
+    const int D = p.D, V = p.V;
+    const int VA = (DELTA && p.mode == 1) ? V + D : V;
+    if (VA > MS_MAX_THREADS) return TTB_ERR_UNSUPPORTED;
     // the fewest rows a thread that still lets a column's row groups fit one block, and at most 512 threads where that works
     int DR = 8;
-    while (DR < 64 && V * ((D + DR - 1) / DR) > 512) DR *= 2;
+    while (DR < 64 && VA * ((D + DR - 1) / DR) > 512) DR *= 2;
     const int R = (D + DR - 1) / DR;
-    if (V * R > MS_MAX_THREADS) return TTB_ERR_UNSUPPORTED;
+    if (VA * R > MS_MAX_THREADS) return TTB_ERR_UNSUPPORTED;
     p.R = R;
-    int threads = (V * R + 31) / 32 * 32;
+    int threads = (VA * R + 31) / 32 * 32;
     if (threads < 64) threads = 64;
-    const size_t smem = ((size_t)MS_TILE * (3 * D + 2 * V) + 2 * (size_t)R * V + MS_TILE + D + 2 * MS_TILE) * sizeof(float);
+    const size_t smem = ((size_t)MS_TILE * (3 * D + 2 * V) + 2 * (size_t)R * (V + (DELTA ? D : 0)) + MS_TILE + D + 2 * MS_TILE) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
-    dim3 grid(segments, p.heads);
+    dim3 grid(segments, p.heads, p.mode == 0 ? 1 : p.parts);
 #define MS_GO(DRV)                                                                                                   \
     do {                                                                                                             \
         static TtbOncePerDevice once;                                                                                \
@@ -370,7 +504,8 @@ static int ms_launch(MsArgs& p, int segments, cudaStream_t stream) {
 TTB_EXPORT int ttb_shifted_state(const void* rkvg, int dtype, long long ld, long long which, const float* log_decay,
                                  const float* bonus, const float* norm_w, float eps, const void* x, long long ldx, int width,
                                  const int* cu_seqlens, const int* slots, float* state, void* kept, void* out, int segments,
-                                 int heads, int dim, int write, cudaStream_t stream) {
+                                 int heads, int dim, int write, int parts, int part_len, float* part_end, float* part_start,
+                                 float* part_log, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
     if (!rkvg || !log_decay || !bonus || !norm_w || !x || !cu_seqlens || !slots || !state || !kept || !out) return TTB_ERR_ARGUMENT;
     if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
@@ -382,17 +517,20 @@ TTB_EXPORT int ttb_shifted_state(const void* rkvg, int dtype, long long ld, long
     p.log_decay = log_decay; p.bonus = bonus; p.norm_w = norm_w; p.eps = eps;
     p.cu_seqlens = cu_seqlens; p.slots = slots; p.state = state; p.kept = kept; p.raw = x; p.ld_raw = ldx; p.width = width;
     p.taps = 2; p.out = out; p.heads = heads; p.kv_heads = heads; p.D = dim; p.V = dim; p.write = write;
+    p.parts = parts; p.part_len = part_len; p.part_end = part_end; p.part_start = part_start; p.part_log = part_log;
     return ms_launch<false>(p, segments, stream);
 }
 
 // conv [T, q | k | v] after the convolutions and their silu (q, k: kv_heads * dim; v: heads * vdim), row stride ld_conv;
 // raw: the convolutions' inputs in the same layout; beta float32 logits [T, heads] (row stride ld_beta); log_decay float32
 // [T, heads * dim]; gate float32 logits [T, heads * vdim]; norm_w float32 [vdim]. state float32 [slots, heads, dim, vdim];
-// kept [slots, taps - 1, channels].
+// kept [slots, taps - 1, channels]. parts > 1: part_end [segments, heads, parts, dim, vdim + dim] and part_start [segments, heads,
+// parts, dim, vdim] are scratch memory (the token-shift state: part_end [.., dim, dim] and part_log [segments, heads, parts, dim]).
 TTB_EXPORT int ttb_delta_rule(const void* conv, int dtype, long long ld_conv, const void* raw, long long ld_raw,
                               const float* beta, int ld_beta, const float* log_decay, const float* gate, const float* norm_w,
                               float eps, const int* cu_seqlens, const int* slots, float* state, void* kept, void* out,
-                              int segments, int heads, int kv_heads, int dim, int vdim, int taps, int write, cudaStream_t stream) {
+                              int segments, int heads, int kv_heads, int dim, int vdim, int taps, int write, int parts, int part_len,
+                              float* part_end, float* part_start, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
     if (!conv || !raw || !beta || !log_decay || !gate || !norm_w || !cu_seqlens || !slots || !state || !out || (taps > 1 && !kept))
         return TTB_ERR_ARGUMENT;
@@ -408,5 +546,6 @@ TTB_EXPORT int ttb_delta_rule(const void* conv, int dtype, long long ld_conv, co
     p.cu_seqlens = cu_seqlens; p.slots = slots; p.state = state; p.kept = kept; p.raw = raw; p.ld_raw = ld_raw;
     p.width = (int)(2 * qk + (long long)heads * vdim); p.taps = taps; p.out = out;
     p.heads = heads; p.kv_heads = kv_heads; p.D = dim; p.V = vdim; p.write = write;
+    p.parts = parts; p.part_len = part_len; p.part_end = part_end; p.part_start = part_start; p.part_log = nullptr;
     return ms_launch<true>(p, segments, stream);
 }

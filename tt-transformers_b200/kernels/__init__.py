@@ -106,7 +106,8 @@ class CudaKernels:
                      "ttb_state_space_scan", "ttb_state_space_supports", "ttb_gate_group_norm", "ttb_state_space_token",
                      "ttb_token_shift", "ttb_lowrank_expand", "ttb_add_row_vector", "ttb_shifted_state", "ttb_delta_rule",
                      "ttb_add_layernorm_sum", "ttb_qk_norm_rope_write_ext", "ttb_paged_attention_generic_bias",
-                     "ttb_latent_prepare_ext", "ttb_latent_attention_generic_ext", "ttb_route_top_corrected"):
+                     "ttb_latent_prepare_ext", "ttb_latent_attention_generic_ext", "ttb_route_top_corrected",
+                     "ttb_paged_attention_mma_bias", "ttb_latent_attention_mma_ext"):
             getattr(self.lib, name).restype = ctypes.c_int
         self.lib.ttb_sample_uniform.restype = ctypes.c_float
         self.lib.ttb_sample_uniform.argtypes = [ctypes.c_longlong, ctypes.c_int]
@@ -763,26 +764,27 @@ class CudaKernels:
         out = torch.empty(T, H, R, dtype=q_latent.dtype, device=self.device)
         if (self.use_mma_latent_attention and q_latent.dtype == torch.bfloat16 and view.rows.is_contiguous() and scale > 0
                 and q_latent.stride(0) % 8 == 0 and q_latent.stride(1) % 8 == 0 and q_latent.data_ptr() % 16 == 0
-                and amplitude == 1.0
                 and self.lib.ttb_latent_attention_mma_supports(R, view.extra, int(rotary_dim), int(window or 0))):
             # tensor cores; few blocks (decode): the keys are split over blocks and merged afterwards
             per_tile = int(self.lib.ttb_latent_attention_mma_tokens_per_tile(H))
             blocks = batch.num_segments * -(-batch.max_seg_len // per_tile) * -(-H // 64) * -(-R // (256 if R > 128 else 128))
             splits = 1
             if blocks < self.sm_count:
-                splits = max(1, min(-(-2 * self.sm_count // blocks), batch.max_context // 128, 64))
+                reach = min(batch.max_context, window + batch.max_seg_len) if window else batch.max_context
+                splits = max(1, min(-(-2 * self.sm_count // blocks), reach // 128, 64))
             partial_o = partial_ml = None
             if splits > 1:
                 partial_o = torch.empty(T * H * splits * R, dtype=torch.float32, device=self.device)
                 partial_ml = torch.empty(T * H * splits * 2, dtype=torch.float32, device=self.device)
-            self._check(self.lib.ttb_latent_attention_mma(
+            self._check(self.lib.ttb_latent_attention_mma_ext(
                 self._p(q_latent), ctypes.c_longlong(q_latent.stride(0)), ctypes.c_longlong(q_latent.stride(1)),
                 self._p(q_rot), ctypes.c_longlong(q_rot.stride(0) if q_rot is not None else 0),
                 ctypes.c_longlong(q_rot.stride(1) if q_rot is not None else 0), self._p(out), self._p(batch.cu_seqlens),
                 self._p(batch.seg_pos0), self._p(view.rows), self._p(view.block_table), view.block_table.shape[1],
                 view.page_size, view.rows.shape[0], batch.num_segments, batch.max_seg_len, T, H, R, view.extra,
                 ctypes.c_float(scale), self._p(sinks), self._p(inv_freq), int(rotary_dim), splits, self._p(partial_o),
-                self._p(partial_ml), 1 if merge else 0, self._p(self.status), self._stream()), "latent_attention_mma")
+                self._p(partial_ml), 1 if merge else 0, self._p(self.status), int(window or 0), ctypes.c_float(amplitude),
+                self._stream()), "latent_attention_mma")
             if splits > 1 and merge:
                 self.launches += 1
             return out, partial_o, partial_ml, splits
@@ -1176,7 +1178,7 @@ class CudaKernels:
             raise KernelError("sink_attention: the bias by distance must be float32 [heads, far + 1]")
         if (self.use_mma_attention and qkv.dtype == torch.bfloat16 and dim == vdim and qkv.stride(0) % 8 == 0
                 and qkv.data_ptr() % 16 == 0 and view.keys.is_contiguous() and view.values.is_contiguous()
-                and distance_bias is None
+                and (distance_bias is None or scale > 0)
                 and self.lib.ttb_attention_mma_supports(heads, kv_heads, dim)):
             # keys and values of one size that the tensor-core kernel takes: 64-row tiles for prompt portions, the
             # decode shape for single tokens; key splits sized by what a query can see at most
@@ -1187,13 +1189,14 @@ class CudaKernels:
             if splits > 1:
                 partial_o = torch.empty(tokens * heads * splits * dim, dtype=torch.float32, device=self.device)
                 partial_ml = torch.empty(tokens * heads * splits * 2, dtype=torch.float32, device=self.device)
-            self._check(self.lib.ttb_paged_attention_mma_ext(
+            self._check(self.lib.ttb_paged_attention_mma_bias(
                 self._p(qkv), qkv.stride(0), self._p(out), self._p(batch.cu_seqlens), self._p(batch.seg_pos0),
                 self._p(view.keys), self._p(view.values), self._p(view.block_table), view.block_table.shape[1],
                 view.page_size, self._p(seg), self._p(tok0), n_tiles, tokens, heads, kv_heads, dim, ctypes.c_float(scale),
                 int(view.window or 0), 1 if decode_shape else 0, splits, self._p(partial_o), self._p(partial_ml),
                 view.keys.shape[0], self._p(self.status), ctypes.c_float(softcap or 0.0), int(view.chunk or 0),
-                self._p(sinks), self._stream()), "sink_attention_mma")
+                self._p(sinks), self._p(distance_bias), distance_bias.shape[1] - 1 if distance_bias is not None else 0,
+                self._stream()), "sink_attention_mma")
             if splits > 1:
                 self.launches += 1
             return out
@@ -1242,6 +1245,27 @@ class CudaKernels:
             T, N, rank, self._stream()), "lowrank_expand")
         return out
 
+    MATRIX_STATE_PART = 64                  # tokens of one part of a long segment in the matrix-state walks
+    MATRIX_STATE_PARTS_FROM = 256           # segments from this many tokens on run as parts side by side
+    MATRIX_STATE_SCRATCH_BYTES = 512 << 20  # most memory for the parts' states; longer parts beyond it
+
+    def _matrix_state_parts(self, batch, heads, rows, cols, cols_end):
+        """How a step's long segments are cut into parts: (parts, part_len, end states, start states) with scratch
+        tensors, or (1, 0, None, None) for steps whose segments are walked whole."""
+        if batch.max_seg_len < self.MATRIX_STATE_PARTS_FROM:
+            return 1, 0, None, None
+        part_len = self.MATRIX_STATE_PART
+        per_part = batch.num_segments * heads * rows * (cols + cols_end) * 4
+        while -(-batch.max_seg_len // part_len) * per_part > self.MATRIX_STATE_SCRATCH_BYTES and part_len < batch.max_seg_len:
+            part_len *= 2
+        parts = -(-batch.max_seg_len // part_len)
+        if parts < 2:
+            return 1, 0, None, None
+        ends = torch.empty(batch.num_segments * heads * parts * rows * cols_end, dtype=torch.float32, device=self.device)
+        starts = torch.empty(batch.num_segments * heads * parts * rows * cols, dtype=torch.float32, device=self.device)
+        self.launches += 2
+        return parts, part_len, ends, starts
+
     def shifted_state(self, rkvg, log_decay, bonus, norm_w, eps, heads, dim, x, batch, view, write_state=True):
         """rkvg [T, 4, heads * dim] (r, k, v and the gate before its silu; any token stride); log_decay float32 [T, heads * dim]
         (ln w, never positive); per head o = (S + diag(bonus) k v^T)^T r, S = diag(w) S + k v^T on the float32 state of
@@ -1255,11 +1279,14 @@ class CudaKernels:
                 or view.tail.dtype != x.dtype or not view.tail.is_contiguous() or x.dtype != rkvg.dtype or x.stride(1) != 1):
             raise KernelError("shifted_state: the state must be float32 [slots, heads, dim, dim], the kept input of the compute dtype")
         out = torch.empty(T, inner, dtype=rkvg.dtype, device=self.device)
+        parts, part_len, ends, starts = self._matrix_state_parts(batch, heads, dim, dim, dim)
+        logs = torch.empty(batch.num_segments * heads * parts * dim, dtype=torch.float32, device=self.device) if parts > 1 else None
         self._check(self.lib.ttb_shifted_state(
             self._p(rkvg), _dtype_code(rkvg.dtype), ctypes.c_longlong(rkvg.stride(0)), ctypes.c_longlong(rkvg.stride(1)),
             self._p(log_decay), self._p(bonus), self._p(norm_w), ctypes.c_float(eps), self._p(x), ctypes.c_longlong(x.stride(0)),
             x.shape[1], self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(out),
-            batch.num_segments, heads, dim, 1 if write_state else 0, self._stream()), "shifted_state")
+            batch.num_segments, heads, dim, 1 if write_state else 0, parts, part_len, self._p(ends), self._p(starts),
+            self._p(logs), self._stream()), "shifted_state")
         return out
 
     def short_conv_silu(self, x, conv_w, batch, view):
@@ -1297,11 +1324,13 @@ class CudaKernels:
                 or view.tail.dtype != u.dtype or not view.tail.is_contiguous() or view.tail.shape[2] != C):
             raise KernelError("delta_rule: the state must be float32 [slots, heads, dim, vdim], the kept inputs of the compute dtype")
         out = torch.empty(T, heads * vdim, dtype=u.dtype, device=self.device)
+        parts, part_len, ends, starts = self._matrix_state_parts(batch, heads, dim, vdim, vdim + dim)
         self._check(self.lib.ttb_delta_rule(
             self._p(u), _dtype_code(u.dtype), ctypes.c_longlong(u.stride(0)), self._p(raw), ctypes.c_longlong(raw.stride(0)),
             self._p(beta), beta.stride(0), self._p(log_decay), self._p(gate), self._p(norm_w), ctypes.c_float(eps),
             self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(out),
-            batch.num_segments, heads, kv_heads, dim, vdim, view.taps, 1 if write_state else 0, self._stream()), "delta_rule")
+            batch.num_segments, heads, kv_heads, dim, vdim, view.taps, 1 if write_state else 0, parts, part_len,
+            self._p(ends), self._p(starts), self._stream()), "delta_rule")
         return out
 
     # ------------------------------------------------------------------ experts chosen from the best groups
