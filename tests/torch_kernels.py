@@ -481,9 +481,10 @@ class TorchKernels:
         return z
 
     def shifted_state(self, rkvg, log_decay, bonus, norm_w, eps, heads, dim, x, batch, view, write_state=True):
-        T = rkvg.shape[0]
-        r, k, v = (rkvg[:, i].float().view(T, heads, dim) for i in range(3))
-        g = rkvg[:, 3].float()
+        four = [rkvg[:, i] for i in range(4)] if torch.is_tensor(rkvg) else list(rkvg)
+        T = four[0].shape[0]
+        r, k, v = (four[i].float().reshape(T, heads, dim) for i in range(3))
+        g = four[3].float()
         w = torch.exp(log_decay).view(T, heads, dim)
         out = torch.empty(T, heads, dim, dtype=torch.float32, device=x.device)
         start = 0

@@ -36,6 +36,13 @@ __device__ __forceinline__ void ms_store(void* p, int dtype, size_t i, float v) 
     else reinterpret_cast<float*>(p)[i] = v;
 }
 __device__ __forceinline__ float ms_sigmoid(float v) { return 1.f / (1.f + expf(-v)); }
+// Four neighbouring values of a row vector in shared memory, rows from `row` on; beyond `rows` zeros (a state row that
+// does not exist is multiplied by zeros and stays zero). vec: the vector is 16-byte aligned at every multiple of four.
+__device__ __forceinline__ float4 ms_row4(const float* v, int row, int rows, bool vec) {
+    if (vec) return row < rows ? *reinterpret_cast<const float4*>(v + row) : make_float4(0.f, 0.f, 0.f, 0.f);
+    return make_float4(row < rows ? v[row] : 0.f, row + 1 < rows ? v[row + 1] : 0.f, row + 2 < rows ? v[row + 2] : 0.f,
+                       row + 3 < rows ? v[row + 3] : 0.f);
+}
 
 // ---------------------------------------------------------------- token shift
 // out[t, s, c] = x[t, c] + (before[t, c] - x[t, c]) * mu[s, c]; before = the segment's token in front, or the request's
@@ -74,40 +81,66 @@ TTB_EXPORT int ttb_token_shift(const void* x, int dtype, int ldx, const float* m
 // ---------------------------------------------------------------- the second half of a low-rank map
 // out[t, n] = f(sum_r act(in[t, r]) W[n, r] + bias[n]), float32 arithmetic; in float32 [tokens, ld_in]; W [N, rank] of
 // the compute type. act: 0 none, 1 tanh. f: 0 z; 1 -exp(z); 2 -rate[n / (N / heads)] * softplus(z).
-#define LR_TOKENS 8
+#define LR_TOKENS 32        // tokens a block
+#define LR_COLS 128         // output columns a block
+#define LR_RANK 64          // the rank in tiles of this many
+// A block of 256 threads takes LR_TOKENS tokens and LR_COLS columns: thread (cn, tg) four columns cn + 32 k and four
+// tokens 4 tg .. 4 tg + 3, sixteen sums in registers; inputs (behind their activation) and weights pass shared memory in
+// tiles of LR_RANK, rows padded by one so that the four columns of a thread lie in different banks.
 __global__ void __launch_bounds__(256)
 lowrank_expand_kernel(const float* __restrict__ in, int ld_in, const void* __restrict__ w, int w_dtype,
                       const float* __restrict__ bias, const float* __restrict__ rate, int per_head, int act, int f,
                       float* __restrict__ out, int tokens, int N, int rank) {
-    extern __shared__ float lr_in[];                 // [LR_TOKENS, rank]
+    __shared__ float xs[LR_TOKENS][LR_RANK + 1];
+    __shared__ float ws[LR_COLS][LR_RANK + 1];
     pdl_wait();
     pdl_launch_dependents();
-    const int t0 = blockIdx.x * LR_TOKENS, nt = min(LR_TOKENS, tokens - t0);
-    for (int i = threadIdx.x; i < LR_TOKENS * rank; i += blockDim.x) {
-        const int tt = i / rank, r = i - tt * rank;
-        float v = tt < nt ? in[(size_t)(t0 + tt) * ld_in + r] : 0.f;
-        lr_in[i] = act == 1 ? tanhf(v) : v;
-    }
-    __syncthreads();
-    for (int n = blockIdx.y * blockDim.x + threadIdx.x; n < N; n += gridDim.y * blockDim.x) {
-        float acc[LR_TOKENS];
+    const int t0 = blockIdx.x * LR_TOKENS, n0 = blockIdx.y * LR_COLS;
+    const int cn = threadIdx.x & 31, tg = threadIdx.x >> 5;
+    float acc[4][4];
 #pragma unroll
-        for (int tt = 0; tt < LR_TOKENS; ++tt) acc[tt] = 0.f;
-        for (int r = 0; r < rank; ++r) {
-            const float wv = ms_load(w, w_dtype, (size_t)n * rank + r);
+    for (int k = 0; k < 4; ++k)
 #pragma unroll
-            for (int tt = 0; tt < LR_TOKENS; ++tt) acc[tt] = fmaf(lr_in[tt * rank + r], wv, acc[tt]);
+        for (int q = 0; q < 4; ++q) acc[k][q] = 0.f;
+    for (int r0 = 0; r0 < rank; r0 += LR_RANK) {
+        const int nr = min(LR_RANK, rank - r0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < LR_TOKENS * nr; i += 256) {
+            const int tt = i / nr, r = i - tt * nr;
+            const float v = t0 + tt < tokens ? in[(size_t)(t0 + tt) * ld_in + r0 + r] : 0.f;
+            xs[tt][r] = act == 1 ? tanhf(v) : v;
         }
+        for (int i = threadIdx.x; i < LR_COLS * nr; i += 256) {
+            const int c = i / nr, r = i - c * nr;
+            ws[c][r] = n0 + c < N ? ms_load(w, w_dtype, (size_t)(n0 + c) * rank + r0 + r) : 0.f;
+        }
+        __syncthreads();
+        for (int r = 0; r < nr; ++r) {
+            float xv[4], wv[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) xv[q] = xs[tg * 4 + q][r];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) wv[k] = ws[cn + 32 * k][r];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[k][q] = fmaf(xv[q], wv[k], acc[k][q]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int n = n0 + cn + 32 * k;
+        if (n >= N) continue;
         const float b = bias != nullptr ? bias[n] : 0.f;
         const float rt = f == 2 ? rate[n / per_head] : 0.f;
 #pragma unroll
-        for (int tt = 0; tt < LR_TOKENS; ++tt) {
-            if (tt < nt) {
-                float z = acc[tt] + b;
-                if (f == 1) z = -expf(z);
-                else if (f == 2) z = -rt * (z > 20.f ? z : log1pf(expf(z)));
-                out[(size_t)(t0 + tt) * N + n] = z;
-            }
+        for (int q = 0; q < 4; ++q) {
+            const int t = t0 + tg * 4 + q;
+            if (t >= tokens) continue;
+            float z = acc[k][q] + b;
+            if (f == 1) z = -expf(z);
+            else if (f == 2) z = -rt * (z > 20.f ? z : log1pf(expf(z)));
+            out[(size_t)t * N + n] = z;
         }
     }
 }
@@ -118,11 +151,10 @@ TTB_EXPORT int ttb_lowrank_expand(const float* in, int ld_in, const void* w, int
     if (!in || !w || !out || rank < 1 || (f == 2 && (!rate || heads < 1 || N % heads))) return TTB_ERR_ARGUMENT;
     if (w_dtype != TTB_DTYPE_BF16 && w_dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
     if (act < 0 || act > 1 || f < 0 || f > 2) return TTB_ERR_UNSUPPORTED;
-    const size_t smem = (size_t)LR_TOKENS * rank * sizeof(float);
-    if (smem > 48 * 1024) return TTB_ERR_UNSUPPORTED;
-    const int by = (N + 255) / 256;
-    dim3 grid((tokens + LR_TOKENS - 1) / LR_TOKENS, by > 64 ? 64 : by);
-    ttb_launch(lowrank_expand_kernel, grid, 256, smem, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
+    const int by = (N + LR_COLS - 1) / LR_COLS;
+    if (by > 65535) return TTB_ERR_UNSUPPORTED;
+    dim3 grid((tokens + LR_TOKENS - 1) / LR_TOKENS, by);
+    ttb_launch(lowrank_expand_kernel, grid, 256, 0, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
                out, tokens, N, rank);
     return ttb_launch_status();
 }
@@ -178,20 +210,20 @@ struct MsArgs {
 
 template <bool DELTA> static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream);
 
-template <int DR, bool DELTA>
-__global__ void __launch_bounds__(DR == 64 ? MS_MAX_THREADS : 512)
+template <int DR, bool DELTA, bool BIG>
+__global__ void __launch_bounds__(BIG ? MS_MAX_THREADS : 512, DR == 8 ? 2 : 1)
 matrix_state_walk_kernel(const MsArgs p) {
     extern __shared__ __align__(16) float ms_smem[];
     const int D = p.D, V = p.V, R = p.R;
     float* sa = ms_smem;                       // [TILE, D]  r or q
     float* sb = sa + MS_TILE * D;              // [TILE, D]  k
     float* sw = sb + MS_TILE * D;              // [TILE, D]  decay
-    float* sc = sw + MS_TILE * D;              // [TILE, V]  v
+    float* sbonus = sw + MS_TILE * D;          // [D]
+    float* sc = sbonus + D;                    // [TILE, V]  v
     float* so = sc + MS_TILE * V;              // [TILE, V]  outputs
     float* part_sums = so + MS_TILE * V;       // [2, R, V (+ D)]
     float* sbeta = part_sums + 2 * R * (V + (DELTA ? D : 0));   // [TILE]
-    float* sbonus = sbeta + MS_TILE;           // [D]
-    float* sscale = sbonus + D;                // [TILE, 2]: unit-norm factors of q and k (delta), then the outputs' norm
+    float* sscale = sbeta + MS_TILE;           // [TILE, 2]: unit-norm factors of q and k (delta), then the outputs' norm
     pdl_wait();
     pdl_launch_dependents();
     const int seg = blockIdx.x, head = blockIdx.y, part = blockIdx.z;
@@ -221,6 +253,7 @@ matrix_state_walk_kernel(const MsArgs p) {
     if (!DELTA)
         for (int d = tid; d < D; d += nthreads) sbonus[d] = p.bonus[(size_t)head * D + d];
     const int lane = tid & 31, warp = tid >> 5, nwarps = nthreads >> 5;
+    const bool vec = (D & 3) == 0;                 // row vectors in shared memory start on 16-byte boundaries
     int turn = 0;
     for (int t0 = t_begin; t0 < t_end; t0 += MS_TILE) {
         const int nt = min(MS_TILE, t_end - t0);
@@ -255,17 +288,21 @@ matrix_state_walk_kernel(const MsArgs p) {
         }
         __syncthreads();
         for (int tt = 0; tt < nt; ++tt) {
-            const float* a = sa + tt * D + row0;
-            const float* b = sb + tt * D + row0;
-            const float* w = sw + tt * D + row0;
+            const float* a = sa + tt * D;
+            const float* b = sb + tt * D;
+            const float* w = sw + tt * D;
             float* mine = part_sums + (size_t)turn * R * VA;
             if (DELTA) {
-                float s = 0.f;
                 if (active) {
+                    float s4[4] = {0.f, 0.f, 0.f, 0.f};          // four chains side by side instead of one of DR links
 #pragma unroll
-                    for (int i = 0; i < DR; ++i)
-                        if (row0 + i < D) { S[i] *= w[i]; s = fmaf(S[i], b[i], s); }
-                    mine[grp * VA + col] = s;
+                    for (int i = 0; i < DR; i += 4) {
+                        const float4 wv = ms_row4(w, row0 + i, D, vec), bv = ms_row4(b, row0 + i, D, vec);
+                        S[i] *= wv.x; S[i + 1] *= wv.y; S[i + 2] *= wv.z; S[i + 3] *= wv.w;
+                        s4[0] = fmaf(S[i], bv.x, s4[0]); s4[1] = fmaf(S[i + 1], bv.y, s4[1]);
+                        s4[2] = fmaf(S[i + 2], bv.z, s4[2]); s4[3] = fmaf(S[i + 3], bv.w, s4[3]);
+                    }
+                    mine[grp * VA + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                 }
                 __syncthreads();
                 float got = 0.f;
@@ -276,16 +313,24 @@ matrix_state_walk_kernel(const MsArgs p) {
                 if (p.mode == 1) {                  // end states only: nobody reads this token's output
                     if (active) {
 #pragma unroll
-                        for (int i = 0; i < DR; ++i)
-                            if (row0 + i < D) S[i] = fmaf(b[i], d, S[i]);
+                        for (int i = 0; i < DR; i += 4) {
+                            const float4 bv = ms_row4(b, row0 + i, D, vec);
+                            S[i] = fmaf(bv.x, d, S[i]); S[i + 1] = fmaf(bv.y, d, S[i + 1]);
+                            S[i + 2] = fmaf(bv.z, d, S[i + 2]); S[i + 3] = fmaf(bv.w, d, S[i + 3]);
+                        }
                     }
                 } else {
-                    s = 0.f;
                     if (active) {
+                        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int i = 0; i < DR; ++i)
-                            if (row0 + i < D) { S[i] = fmaf(b[i], d, S[i]); s = fmaf(S[i], a[i], s); }
-                        mine[grp * VA + col] = s;
+                        for (int i = 0; i < DR; i += 4) {
+                            const float4 bv = ms_row4(b, row0 + i, D, vec), av = ms_row4(a, row0 + i, D, vec);
+                            S[i] = fmaf(bv.x, d, S[i]); S[i + 1] = fmaf(bv.y, d, S[i + 1]);
+                            S[i + 2] = fmaf(bv.z, d, S[i + 2]); S[i + 3] = fmaf(bv.w, d, S[i + 3]);
+                            s4[0] = fmaf(S[i], av.x, s4[0]); s4[1] = fmaf(S[i + 1], av.y, s4[1]);
+                            s4[2] = fmaf(S[i + 2], av.z, s4[2]); s4[3] = fmaf(S[i + 3], av.w, s4[3]);
+                        }
+                        mine[grp * VA + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                     }
                     __syncthreads();
                     if (grp == 0) {
@@ -300,22 +345,27 @@ matrix_state_walk_kernel(const MsArgs p) {
                 if (p.mode == 1) {                  // end states only
                     if (active) {
 #pragma unroll
-                        for (int i = 0; i < DR; ++i)
-                            if (row0 + i < D) S[i] = fmaf(w[i], S[i], b[i] * vc);
+                        for (int i = 0; i < DR; i += 4) {
+                            const float4 wv = ms_row4(w, row0 + i, D, vec), bv = ms_row4(b, row0 + i, D, vec);
+                            S[i] = fmaf(wv.x, S[i], bv.x * vc); S[i + 1] = fmaf(wv.y, S[i + 1], bv.y * vc);
+                            S[i + 2] = fmaf(wv.z, S[i + 2], bv.z * vc); S[i + 3] = fmaf(wv.w, S[i + 3], bv.w * vc);
+                        }
                     }
                     continue;
                 }
-                float s = 0.f;
                 if (active) {
+                    float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                    for (int i = 0; i < DR; ++i) {
-                        if (row0 + i < D) {
-                            const float kv = b[i] * vc;
-                            s = fmaf(a[i], fmaf(sbonus[row0 + i], kv, S[i]), s);
-                            S[i] = fmaf(w[i], S[i], kv);
-                        }
+                    for (int i = 0; i < DR; i += 4) {
+                        const float4 wv = ms_row4(w, row0 + i, D, vec), bv = ms_row4(b, row0 + i, D, vec);
+                        const float4 av = ms_row4(a, row0 + i, D, vec), uv = ms_row4(sbonus, row0 + i, D, vec);
+                        const float k0 = bv.x * vc, k1 = bv.y * vc, k2 = bv.z * vc, k3 = bv.w * vc;
+                        s4[0] = fmaf(av.x, fmaf(uv.x, k0, S[i]), s4[0]); s4[1] = fmaf(av.y, fmaf(uv.y, k1, S[i + 1]), s4[1]);
+                        s4[2] = fmaf(av.z, fmaf(uv.z, k2, S[i + 2]), s4[2]); s4[3] = fmaf(av.w, fmaf(uv.w, k3, S[i + 3]), s4[3]);
+                        S[i] = fmaf(wv.x, S[i], k0); S[i + 1] = fmaf(wv.y, S[i + 1], k1);
+                        S[i + 2] = fmaf(wv.z, S[i + 2], k2); S[i + 3] = fmaf(wv.w, S[i + 3], k3);
                     }
-                    mine[grp * V + col] = s;
+                    mine[grp * V + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                 }
                 __syncthreads();
                 if (grp == 0) {
@@ -394,50 +444,107 @@ matrix_state_walk_kernel(const MsArgs p) {
     }
 }
 
-// The parts folded in order: S_0 = the request's state; S_(p+1) = M_p S_p + E_p. A block per (segment, head); the state
-// in shared memory, twice for the delta rule (the new one is a product with the old one). Leaves every part's start state
-// in part_start and, with `write`, the state behind the last part in the request's slot.
-template <bool DELTA>
+// The parts folded in order: S_0 = the request's state; S_(p+1) = M_p S_p + E_p. Columns of the state do not mix, and with
+// a diagonal M nothing does: the token-shift state folds element by element (a thread per element, blocks of 256), the
+// delta rule in tiles of FOLD_COLS columns per block with M_p staged in shared memory. Leaves every part's start state in
+// part_start and, with `write`, the state behind the last part in the request's slot.
+#define FOLD_COLS 16
 __global__ void __launch_bounds__(256)
-matrix_state_fold_kernel(const MsArgs p) {
-    extern __shared__ __align__(16) float fold_smem[];
+matrix_state_fold_diagonal_kernel(const MsArgs p) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int D = p.D, V = p.V, n = D * V;
-    float* cur = fold_smem;
-    float* next = fold_smem + n;                   // delta rule only
+    const int seg = blockIdx.x, head = blockIdx.y, i = blockIdx.z * 256 + threadIdx.x;
+    const int len = p.cu_seqlens[seg + 1] - p.cu_seqlens[seg];
+    if (len == 0 || i >= n) return;
+    const int nparts = (len + p.part_len - 1) / p.part_len;
+    float* state = p.state + ((size_t)p.slots[seg] * p.heads + head) * n;
+    float cur = state[i];
+    const size_t first = ((size_t)seg * p.heads + head) * p.parts;
+    for (int part = 0; part < nparts; ++part) {
+        p.part_start[(first + part) * n + i] = cur;
+        cur = fmaf(expf(p.part_log[(first + part) * D + i / V]), cur, p.part_end[(first + part) * n + i]);
+    }
+    if (p.write) state[i] = cur;
+}
+
+// `buffers` 2: M of the next part is on its way (asynchronous copies) while this part is multiplied; 1: one at a time.
+__global__ void __launch_bounds__(256)
+matrix_state_fold_kernel(const MsArgs p, int buffers) {
+    extern __shared__ __align__(16) float fold_smem[];
+    const int D = p.D, V = p.V, n = D * V, VA = V + D, m_size = D * (D + 1);
+    float* M = fold_smem;                          // [buffers][D, D + 1]
+    float* cur = M + (size_t)buffers * m_size;     // [D, FOLD_COLS]
+    float* next = cur + D * FOLD_COLS;
     pdl_wait();
     pdl_launch_dependents();
     const int seg = blockIdx.x, head = blockIdx.y, tid = threadIdx.x;
+    const int c0 = blockIdx.z * FOLD_COLS, ncols = min(FOLD_COLS, V - c0);
     const int len = p.cu_seqlens[seg + 1] - p.cu_seqlens[seg];
     if (len == 0) return;
     const int nparts = (len + p.part_len - 1) / p.part_len;
+    const size_t first = ((size_t)seg * p.heads + head) * p.parts;
     float* state = p.state + ((size_t)p.slots[seg] * p.heads + head) * n;
-    for (int i = tid; i < n; i += blockDim.x) cur[i] = state[i];
-    __syncthreads();
-    for (int part = 0; part < nparts; ++part) {
-        const size_t index = ((size_t)seg * p.heads + head) * p.parts + part;
-        float* begin = p.part_start + index * n;
-        for (int i = tid; i < n; i += blockDim.x) begin[i] = cur[i];
-        if (DELTA) {
-            const int VA = V + D;
-            const float* end = p.part_end + index * D * VA;           // row r: [E (V) | M (D)]
-            for (int i = tid; i < n; i += blockDim.x) {
-                const int r = i / V, c = i - r * V;
-                const float* row = end + (size_t)r * VA;
-                float acc = row[c];
-                for (int j = 0; j < D; ++j) acc = fmaf(row[V + j], cur[j * V + c], acc);
-                next[i] = acc;
-            }
-            __syncthreads();
-            float* t = cur; cur = next; next = t;
-        } else {
-            const float* end = p.part_end + index * n;
-            const float* logs = p.part_log + index * D;
-            for (int i = tid; i < n; i += blockDim.x) cur[i] = fmaf(expf(logs[i / V]), cur[i], end[i]);
-            __syncthreads();
+    auto fetch = [&](int part) {                   // M_part into its buffer, four bytes a copy (rows are padded by one)
+        const float* end = p.part_end + (first + part) * D * VA;
+        float* dst = M + (size_t)(buffers == 2 ? (part & 1) : 0) * m_size;
+        for (int i = tid; i < D * D; i += blockDim.x) {
+            const int r = i / D, j = i - r * D;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst + r * (D + 1) + j);
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(end + (size_t)r * VA + V + j) : "memory");
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    fetch(0);
+    for (int e = tid; e < D * FOLD_COLS; e += blockDim.x) {          // columns beyond the state's are zeros and stay zeros
+        const int r = e / FOLD_COLS, c = e - r * FOLD_COLS;
+        cur[e] = c < ncols ? state[(size_t)r * V + c0 + c] : 0.f;
+        next[e] = 0.f;
+    }
+    for (int part = 0; part < nparts; ++part) {
+        if (buffers == 2 && part + 1 < nparts) {
+            fetch(part + 1);                       // the buffer of part - 1: everybody is past its products (the barrier below)
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();                           // M_part and the state before the part are in place
+        const float* Mp = M + (size_t)(buffers == 2 ? (part & 1) : 0) * m_size;
+        const float* end = p.part_end + (first + part) * D * VA;     // row r: [E (V) | M (D)]
+        float* begin = p.part_start + (first + part) * n;
+        // a thread takes four neighbouring columns of one row: a number of M serves four products
+        for (int e = tid; e < D * (FOLD_COLS / 4); e += blockDim.x) {
+            const int r = e / (FOLD_COLS / 4), c = (e - r * (FOLD_COLS / 4)) * 4;
+            if (c >= ncols) continue;
+            const float4 before = *reinterpret_cast<const float4*>(cur + r * FOLD_COLS + c);
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            const float* row = Mp + r * (D + 1);
+            for (int j = 0; j < D; ++j) {
+                const float m = row[j];
+                const float4 sv = *reinterpret_cast<const float4*>(cur + j * FOLD_COLS + c);
+                acc[0] = fmaf(m, sv.x, acc[0]); acc[1] = fmaf(m, sv.y, acc[1]);
+                acc[2] = fmaf(m, sv.z, acc[2]); acc[3] = fmaf(m, sv.w, acc[3]);
+            }
+            const float was[4] = {before.x, before.y, before.z, before.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float v = 0.f;
+                if (c + q < ncols) {
+                    begin[(size_t)r * V + c0 + c + q] = was[q];
+                    v = end[(size_t)r * VA + c0 + c + q] + acc[q];
+                }
+                next[r * FOLD_COLS + c + q] = v;
+            }
+        }
+        __syncthreads();
+        float* t = cur; cur = next; next = t;
+        if (buffers == 1 && part + 1 < nparts) fetch(part + 1);
     }
     if (p.write)
-        for (int i = tid; i < n; i += blockDim.x) state[i] = cur[i];
+        for (int e = tid; e < D * ncols; e += blockDim.x) {
+            const int r = e / ncols, c = e - r * ncols;
+            state[(size_t)r * V + c0 + c] = cur[r * FOLD_COLS + c];
+        }
 }
 
 template <bool DELTA>
@@ -446,18 +553,29 @@ static int ms_launch(MsArgs& p, int segments, cudaStream_t stream) {
     if (D < 1 || V < 1 || V > MS_MAX_THREADS || p.heads < 1 || p.heads > 65535) return TTB_ERR_UNSUPPORTED;
     if (p.parts > 1) {
         if (!p.part_end || !p.part_start || (!DELTA && !p.part_log) || p.part_len < 1 || p.parts > 65535) return TTB_ERR_ARGUMENT;
-        const size_t fold_smem = (size_t)(DELTA ? 2 : 1) * D * V * sizeof(float);
-        if (fold_smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+        const size_t one_m = (size_t)D * (D + 1) * sizeof(float), states = 2 * (size_t)D * FOLD_COLS * sizeof(float);
+        const int fold_buffers = 2 * one_m + states <= 200 * 1024 ? 2 : 1;
+        const size_t fold_smem = DELTA ? fold_buffers * one_m + states : 0;
+        if (fold_smem > 200 * 1024 || (DELTA && V + D > MS_MAX_THREADS)) {      // too large a transition: the walk as a whole
+            p.mode = 0;
+            p.parts = 1;
+            return ms_launch_mode<DELTA>(p, segments, stream);
+        }
         MsArgs ends = p;
         ends.mode = 1;
         int rc = ms_launch_mode<DELTA>(ends, segments, stream);
         if (rc != TTB_OK) return rc;
-        static TtbOncePerDevice once;
-        if (fold_smem > 48 * 1024 && once.pending()) {
-            cudaFuncSetAttribute(matrix_state_fold_kernel<DELTA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            once.mark();
+        if (DELTA) {
+            static TtbOncePerDevice once;
+            if (fold_smem > 48 * 1024 && once.pending()) {
+                cudaFuncSetAttribute(matrix_state_fold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                once.mark();
+            }
+            ttb_launch(matrix_state_fold_kernel, dim3(segments, p.heads, (V + FOLD_COLS - 1) / FOLD_COLS), 256, fold_smem, stream, p,
+                       fold_buffers);
+        } else {
+            ttb_launch(matrix_state_fold_diagonal_kernel, dim3(segments, p.heads, (D * V + 255) / 256), 256, 0, stream, p);
         }
-        ttb_launch(matrix_state_fold_kernel<DELTA>, dim3(segments, p.heads), 256, fold_smem, stream, p);
         rc = ttb_launch_status();
         if (rc != TTB_OK) return rc;
         p.mode = 2;
@@ -484,34 +602,35 @@ static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream) {
     const size_t smem = ((size_t)MS_TILE * (3 * D + 2 * V) + 2 * (size_t)R * (V + (DELTA ? D : 0)) + MS_TILE + D + 2 * MS_TILE) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     dim3 grid(segments, p.heads, p.mode == 0 ? 1 : p.parts);
-#define MS_GO(DRV)                                                                                                   \
+#define MS_GO(DRV, BIGV)                                                                                             \
     do {                                                                                                             \
         static TtbOncePerDevice once;                                                                                \
         if (smem > 48 * 1024 && once.pending()) {                                                                    \
-            cudaFuncSetAttribute(matrix_state_walk_kernel<DRV, DELTA>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+            cudaFuncSetAttribute(matrix_state_walk_kernel<DRV, DELTA, BIGV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
             once.mark();                                                                                             \
         }                                                                                                            \
-        ttb_launch(matrix_state_walk_kernel<DRV, DELTA>, grid, threads, smem, stream, p);                            \
+        ttb_launch(matrix_state_walk_kernel<DRV, DELTA, BIGV>, grid, threads, smem, stream, p);                      \
     } while (0)
-    if (DR == 8) MS_GO(8); else if (DR == 16) MS_GO(16); else if (DR == 32) MS_GO(32); else MS_GO(64);
+    // more than 512 threads only where sixty-four rows a thread still leave that many columns and row groups
+    if (DR == 8) MS_GO(8, false); else if (DR == 16) MS_GO(16, false); else if (DR == 32) MS_GO(32, false);
+    else if (threads <= 512) MS_GO(64, false); else MS_GO(64, true);
 #undef MS_GO
     return ttb_launch_status();
 }
 
-// rkvg: r, k, v and the gate [T, heads * dim] each, of the compute type, with a common row stride `ld` and `which` elements
-// between one and the next. log_decay float32 [T, heads * dim]; bonus float32 [heads, dim]; norm_w float32 [heads * dim].
+// r, k, v and the gate (before its silu): [T, heads * dim] each, of the compute type, with a common row stride `ld`.
+// log_decay float32 [T, heads * dim]; bonus float32 [heads, dim]; norm_w float32 [heads * dim].
 // state float32 [slots, heads, dim, dim]; kept [slots, width]: the request's last input, refreshed from x [T, ldx].
-TTB_EXPORT int ttb_shifted_state(const void* rkvg, int dtype, long long ld, long long which, const float* log_decay,
+TTB_EXPORT int ttb_shifted_state(const void* r, const void* k, const void* v, const void* g, int dtype, long long ld, const float* log_decay,
                                  const float* bonus, const float* norm_w, float eps, const void* x, long long ldx, int width,
                                  const int* cu_seqlens, const int* slots, float* state, void* kept, void* out, int segments,
                                  int heads, int dim, int write, int parts, int part_len, float* part_end, float* part_start,
                                  float* part_log, cudaStream_t stream) {
     if (segments == 0) return TTB_OK;
-    if (!rkvg || !log_decay || !bonus || !norm_w || !x || !cu_seqlens || !slots || !state || !kept || !out) return TTB_ERR_ARGUMENT;
+    if (!r || !k || !v || !g || !log_decay || !bonus || !norm_w || !x || !cu_seqlens || !slots || !state || !kept || !out) return TTB_ERR_ARGUMENT;
     if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
-    const size_t el = dtype == TTB_DTYPE_BF16 ? 2 : 4;
     MsArgs p = {};
-    p.a = rkvg; p.b = (const char*)rkvg + which * el; p.c = (const char*)rkvg + 2 * which * el; p.gate = (const char*)rkvg + 3 * which * el;
+    p.a = r; p.b = k; p.c = v; p.gate = g;
     p.ld_a = p.ld_b = p.ld_c = p.ld_gate = ld;
     p.dtype = p.gate_dtype = dtype;
     p.log_decay = log_decay; p.bonus = bonus; p.norm_w = norm_w; p.eps = eps;

@@ -1267,22 +1267,25 @@ class CudaKernels:
         return parts, part_len, ends, starts
 
     def shifted_state(self, rkvg, log_decay, bonus, norm_w, eps, heads, dim, x, batch, view, write_state=True):
-        """rkvg [T, 4, heads * dim] (r, k, v and the gate before its silu; any token stride); log_decay float32 [T, heads * dim]
+        """rkvg [T, 4, heads * dim] (r, k, v and the gate before its silu; any token stride), or those four as separate
+        tensors [T, heads * dim] with one row stride; log_decay float32 [T, heads * dim]
         (ln w, never positive); per head o = (S + diag(bonus) k v^T)^T r, S = diag(w) S + k v^T on the float32 state of
         view.state; then o / rms(o) per head, times norm_w, times silu(gate) -> [T, heads * dim]. Leaves the state and the
         request's last input (x's last row of the segment) in the request's slot."""
-        T = rkvg.shape[0]
         inner = heads * dim
-        if rkvg.shape[1:] != (4, inner) or rkvg.stride(2) != 1 or log_decay.dtype != torch.float32 or not log_decay.is_contiguous():
-            raise KernelError("shifted_state: rkvg [T, 4, heads * dim] contiguous along its last axis, float32 decays")
+        four = [rkvg[:, i] for i in range(4)] if torch.is_tensor(rkvg) else list(rkvg)
+        T, dtype, ld = four[0].shape[0], four[0].dtype, four[0].stride(0)
+        if (len(four) != 4 or any(t.shape != (T, inner) or t.stride(1) != 1 or t.stride(0) != ld or t.dtype != dtype for t in four)
+                or log_decay.dtype != torch.float32 or not log_decay.is_contiguous()):
+            raise KernelError("shifted_state: r, k, v and the gate [T, heads * dim] with one row stride, float32 decays")
         if (view.state.dtype != torch.float32 or tuple(view.state.shape[1:]) != (heads, dim, dim) or not view.state.is_contiguous()
-                or view.tail.dtype != x.dtype or not view.tail.is_contiguous() or x.dtype != rkvg.dtype or x.stride(1) != 1):
+                or view.tail.dtype != x.dtype or not view.tail.is_contiguous() or x.dtype != dtype or x.stride(1) != 1):
             raise KernelError("shifted_state: the state must be float32 [slots, heads, dim, dim], the kept input of the compute dtype")
-        out = torch.empty(T, inner, dtype=rkvg.dtype, device=self.device)
+        out = torch.empty(T, inner, dtype=dtype, device=self.device)
         parts, part_len, ends, starts = self._matrix_state_parts(batch, heads, dim, dim, dim)
         logs = torch.empty(batch.num_segments * heads * parts * dim, dtype=torch.float32, device=self.device) if parts > 1 else None
         self._check(self.lib.ttb_shifted_state(
-            self._p(rkvg), _dtype_code(rkvg.dtype), ctypes.c_longlong(rkvg.stride(0)), ctypes.c_longlong(rkvg.stride(1)),
+            self._p(four[0]), self._p(four[1]), self._p(four[2]), self._p(four[3]), _dtype_code(dtype), ctypes.c_longlong(ld),
             self._p(log_decay), self._p(bonus), self._p(norm_w), ctypes.c_float(eps), self._p(x), ctypes.c_longlong(x.stride(0)),
             x.shape[1], self._p(batch.cu_seqlens), self._p(view.slots), self._p(view.state), self._p(view.tail), self._p(out),
             batch.num_segments, heads, dim, 1 if write_state else 0, parts, part_len, self._p(ends), self._p(starts),

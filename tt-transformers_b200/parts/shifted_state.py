@@ -26,6 +26,7 @@ MIXES = ("r", "k", "v", "g", "w")
 
 class ShiftedState(Mixer):
     graph_safe = True
+    SKINNY_ROWS = 16        # up to this many tokens the four projections run one by one
 
     def __init__(self, width: int, heads: int, dim: int, eps: float, prefix: str, decay_rank: Optional[int] = None,
                  position=None):
@@ -61,7 +62,11 @@ class ShiftedState(Mixer):
     def forward(self, x, batch, cache, write_cache=True):
         k = self.runtime.kernels
         mixes = k.token_shift(x, self.mu, batch, cache)                                      # [T, 5, width]
-        rkvg = k.heads_linear(mixes[:, :4], self.w_rkvg)                                     # [T, 4, inner]
+        if x.shape[0] <= self.SKINNY_ROWS:
+            # a handful of tokens: four products that stream their weights, each by the kernel made for few rows
+            rkvg = [k.linear(mixes[:, i], self.w_rkvg[i]) for i in range(4)]
+        else:
+            rkvg = k.heads_linear(mixes[:, :4], self.w_rkvg)                                 # [T, 4, inner]
         low = k.linear(mixes[:, 4], self.w_1, out_dtype=torch.float32)                       # [T, rank]
         log_decay = k.lowrank_expand(low, self.w_2, self.w_0, "tanh", "neg_exp")             # float32 [T, inner] = ln w
         mixed = k.shifted_state(rkvg, log_decay, self.bonus, self.norm, self.eps, self.heads, self.dim, x, batch, cache,
