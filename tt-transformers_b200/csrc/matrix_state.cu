@@ -82,53 +82,61 @@ TTB_EXPORT int ttb_token_shift(const void* x, int dtype, int ldx, const float* m
 // out[t, n] = f(sum_r act(in[t, r]) W[n, r] + bias[n]), float32 arithmetic; in float32 [tokens, ld_in]; W [N, rank] of
 // the compute type. act: 0 none, 1 tanh. f: 0 z; 1 -exp(z); 2 -rate[n / (N / heads)] * softplus(z).
 #define LR_TOKENS 32        // tokens a block
-#define LR_COLS 128         // output columns a block
 #define LR_RANK 64          // the rank in tiles of this many
-// A block of 256 threads takes LR_TOKENS tokens and LR_COLS columns: thread (cn, tg) four columns cn + 32 k and four
-// tokens 4 tg .. 4 tg + 3, sixteen sums in registers; inputs (behind their activation) and weights pass shared memory in
-// tiles of LR_RANK, rows padded by one so that the four columns of a thread lie in different banks.
+#define LR_LD (LR_RANK + 4) // a row in shared memory: 16-byte aligned, and the eight threads of a vector load in different banks
+// A block of 256 threads takes LR_TOKENS tokens and 32 CPT columns: thread (cn, tg) the columns cn + 32 k (k < CPT) and the
+// tokens 4 tg .. 4 tg + 3, 4 CPT sums in registers; inputs (behind their activation) and weights pass shared memory in
+// tiles of LR_RANK and are read four values a load. CPT 4 for prompt portions, 1 for a handful of tokens (more blocks,
+// fewer loads in a row before the first product).
+template <int CPT>
 __global__ void __launch_bounds__(256)
 lowrank_expand_kernel(const float* __restrict__ in, int ld_in, const void* __restrict__ w, int w_dtype,
                       const float* __restrict__ bias, const float* __restrict__ rate, int per_head, int act, int f,
                       float* __restrict__ out, int tokens, int N, int rank) {
-    __shared__ float xs[LR_TOKENS][LR_RANK + 1];
-    __shared__ float ws[LR_COLS][LR_RANK + 1];
+    constexpr int COLS = 32 * CPT;
+    __shared__ __align__(16) float xs[LR_TOKENS][LR_LD];
+    __shared__ __align__(16) float ws[COLS][LR_LD];
     pdl_wait();
     pdl_launch_dependents();
-    const int t0 = blockIdx.x * LR_TOKENS, n0 = blockIdx.y * LR_COLS;
+    const int t0 = blockIdx.x * LR_TOKENS, n0 = blockIdx.y * COLS;
     const int cn = threadIdx.x & 31, tg = threadIdx.x >> 5;
-    float acc[4][4];
+    float acc[CPT][4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
+    for (int k = 0; k < CPT; ++k)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[k][q] = 0.f;
     for (int r0 = 0; r0 < rank; r0 += LR_RANK) {
         const int nr = min(LR_RANK, rank - r0);
         __syncthreads();
-        for (int i = threadIdx.x; i < LR_TOKENS * nr; i += 256) {
-            const int tt = i / nr, r = i - tt * nr;
-            const float v = t0 + tt < tokens ? in[(size_t)(t0 + tt) * ld_in + r0 + r] : 0.f;
+        // tiles are filled to LR_RANK with zeros, so that the products need no bound
+#pragma unroll 4
+        for (int i = threadIdx.x; i < LR_TOKENS * LR_RANK; i += 256) {
+            const int tt = i / LR_RANK, r = i - tt * LR_RANK;
+            const float v = (t0 + tt < tokens && r < nr) ? in[(size_t)(t0 + tt) * ld_in + r0 + r] : 0.f;
             xs[tt][r] = act == 1 ? tanhf(v) : v;
         }
-        for (int i = threadIdx.x; i < LR_COLS * nr; i += 256) {
-            const int c = i / nr, r = i - c * nr;
-            ws[c][r] = n0 + c < N ? ms_load(w, w_dtype, (size_t)(n0 + c) * rank + r0 + r) : 0.f;
+#pragma unroll 8
+        for (int i = threadIdx.x; i < COLS * LR_RANK; i += 256) {
+            const int c = i / LR_RANK, r = i - c * LR_RANK;
+            ws[c][r] = (n0 + c < N && r < nr) ? ms_load(w, w_dtype, (size_t)(n0 + c) * rank + r0 + r) : 0.f;
         }
         __syncthreads();
-        for (int r = 0; r < nr; ++r) {
-            float xv[4], wv[4];
+#pragma unroll 4
+        for (int r = 0; r < LR_RANK; r += 4) {
+            float4 xv[4], wv[CPT];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) xv[q] = xs[tg * 4 + q][r];
+            for (int q = 0; q < 4; ++q) xv[q] = *reinterpret_cast<const float4*>(&xs[tg * 4 + q][r]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) wv[k] = ws[cn + 32 * k][r];
+            for (int k = 0; k < CPT; ++k) wv[k] = *reinterpret_cast<const float4*>(&ws[cn + 32 * k][r]);
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
+            for (int k = 0; k < CPT; ++k)
 #pragma unroll
-                for (int q = 0; q < 4; ++q) acc[k][q] = fmaf(xv[q], wv[k], acc[k][q]);
+                for (int q = 0; q < 4; ++q)
+                    acc[k][q] = fmaf(xv[q].w, wv[k].w, fmaf(xv[q].z, wv[k].z, fmaf(xv[q].y, wv[k].y, fmaf(xv[q].x, wv[k].x, acc[k][q]))));
         }
     }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < CPT; ++k) {
         const int n = n0 + cn + 32 * k;
         if (n >= N) continue;
         const float b = bias != nullptr ? bias[n] : 0.f;
@@ -151,11 +159,16 @@ TTB_EXPORT int ttb_lowrank_expand(const float* in, int ld_in, const void* w, int
     if (!in || !w || !out || rank < 1 || (f == 2 && (!rate || heads < 1 || N % heads))) return TTB_ERR_ARGUMENT;
     if (w_dtype != TTB_DTYPE_BF16 && w_dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
     if (act < 0 || act > 1 || f < 0 || f > 2) return TTB_ERR_UNSUPPORTED;
-    const int by = (N + LR_COLS - 1) / LR_COLS;
+    const int cpt = tokens <= 2 * LR_TOKENS ? 1 : 4;
+    const int by = (N + 32 * cpt - 1) / (32 * cpt);
     if (by > 65535) return TTB_ERR_UNSUPPORTED;
     dim3 grid((tokens + LR_TOKENS - 1) / LR_TOKENS, by);
-    ttb_launch(lowrank_expand_kernel, grid, 256, 0, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
-               out, tokens, N, rank);
+    if (cpt == 1)
+        ttb_launch(lowrank_expand_kernel<1>, grid, 256, 0, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
+                   out, tokens, N, rank);
+    else
+        ttb_launch(lowrank_expand_kernel<4>, grid, 256, 0, stream, in, ld_in, w, w_dtype, bias, rate, f == 2 ? N / heads : 1, act, f,
+                   out, tokens, N, rank);
     return ttb_launch_status();
 }
 
