@@ -185,3 +185,55 @@ def read_folder(folder):
         for name in f.keys():
             w[name] = f.get_tensor(name).to(torch.float32)
     return cfg, w
+
+
+def random_config(seed):
+    """A configuration drawn from a seed: sizes, head counts, layer order, windows, ranks, taps and constants all vary;
+    layers that read another layer's latent appear where an owner with the same latent sizes stands before them."""
+    import random
+
+    rng = random.Random(seed)
+    pick = rng.choice
+    width = pick([40, 64, 96, 136, 200, 256])
+
+    def some_mlp():
+        kind = pick(["none", "dense", "moe", "moe"])
+        if kind == "none":
+            return None
+        if kind == "dense":
+            return dense(pick([24, 70, 128, 264]))
+        experts = pick([1, 2, 5, 8, 12, 16])
+        return moe(experts, rng.randint(1, min(experts, 4)), pick([8, 24, 40, 64]), scale=pick([1.0, 0.6, 2.5]),
+                   shared=pick([None, 16, 56]))
+
+    families = []                       # latent sizes that owners of a latent have used so far: (layer, kv_rank, rot_dim, rot keys)
+    layers = []
+    for i in range(rng.randint(2, 7)):
+        kind = pick(["delta", "side", "latent", "latent"])
+        if kind == "delta":
+            kv = pick([1, 2, 3])
+            mixer = delta(kv * pick([1, 2, 4]), kv, pick([4, 8, 24, 32, 64]), pick([8, 16, 40, 64]), taps=rng.randint(1, 5),
+                          decay_rank=rng.randint(1, 24), gate_rank=rng.randint(1, 24))
+        elif kind == "side":
+            kv = pick([1, 2, 3])
+            dim = pick([8, 16, 24, 64, 128])
+            rows = pick([2, 4, 6, 10, 16, 32])
+            mixer = side_by_side(kv * pick([1, 2, 4]), kv, dim, pick([dim, dim, 8, 48]), bias_rows=rows,
+                                 bias_max=rows // 2 + rng.randint(1, 150), state_heads=rng.randint(1, 4), state_dim=pick([4, 8, 20, 32, 64]),
+                                 scale=pick([None, 0.3, 1.1]), softcap=pick([None, 8.0, 30.0]), temp=pick([None, (0.5, 16), (0.2, 3)]),
+                                 left_scale=pick([1.0, 0.6]), right_scale=pick([1.0, 0.45]), decay_rank=rng.randint(1, 20))
+        else:
+            heads, dim, vdim = pick([1, 2, 4, 5, 8]), pick([8, 16, 32, 64]), pick([8, 16, 24, 64])
+            window = pick([None, 1, 5, 33, 64, 150])
+            if families and rng.random() < 0.5:
+                owner, kv_rank, rot_dim, rot = pick(families)
+                mixer = latent(heads, dim, rot_dim, vdim, kv_rank, window, kv_from=owner)
+                if rot is not None:
+                    mixer["mixer"]["rot"] = copy.deepcopy(rot)
+            else:
+                rot_dim = pick([0, 4, 16, 32, 64])
+                mixer = latent(heads, dim, rot_dim, vdim, pick([16, 24, 48, 64, 128]), window, base=pick([100.0, 10000.0]),
+                               scaling=pick([None, (4.0, 64, 8.0, 1.0), (2.0, 32, 4.0, 0.5)]))
+                families.append((i, mixer["mixer"]["kv_rank"], rot_dim, mixer["mixer"].get("rot")))
+        layers.append(layer(mixer, some_mlp()))
+    return config(width, rng.randint(50, 700), layers, eps=pick([1e-5, 1e-6]), mult=pick([1.0, 0.5, 0.8]), embed=pick([None, 2.0, 9.0]))

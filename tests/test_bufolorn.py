@@ -123,6 +123,24 @@ def test_engine_with_plain_twins_matches_the_plain_implementation(tmp_path, name
             assert helpers.relative_error(got[rid], ref[rid]) < 3e-5, (make_steps.__name__, rid)
 
 
+@pytest.mark.parametrize("seed", [2, 5, 11])
+def test_configurations_drawn_from_a_seed(tmp_path, seed):
+    """Sizes, head counts, layer order, windows, ranks, taps and constants that nobody chose by hand."""
+    folder = cases.write_folder(str(tmp_path / "m"), cases.random_config(seed), seed=seed)
+    cfg, w = cases.read_folder(folder)
+    requests = {f"r{i}": helpers.random_tokens(cfg["vocab"], n, seed * 10 + i) for i, n in enumerate((33, 1, 70, 9, 2))}
+    ref = {rid: _plain(cfg, w, toks) for rid, toks in requests.items()}
+    for make_steps in (helpers.steps_whole, helpers.steps_mixed):
+        steps = make_steps(requests)
+        pages = -(-helpers.max_live_tokens(requests, steps, rounding=4) // 4)
+        engine = _engine(folder, pages=pages)
+        _poison(engine)
+        got = helpers.run_steps(engine, steps)
+        engine.cache.audit()
+        for rid in ref:
+            assert helpers.relative_error(got[rid], ref[rid]) < 5e-5, (make_steps.__name__, rid)
+
+
 def test_token_by_token_from_the_first_token_and_a_long_decoded_tail(tmp_path):
     folder = cases.write_folder(str(tmp_path / "m"), cases.ALIGNED, seed=5)
     cfg, w = cases.read_folder(folder)

@@ -392,6 +392,35 @@ def test_engine_matches_the_plain_implementation(tmp_path, dtype, tol, name):
             engine.close()
 
 
+@pytest.mark.parametrize("seed", [1, 4, 7, 10, 12, 15])
+def test_configurations_drawn_from_a_seed(tmp_path, seed):
+    """Sizes, head counts, layer order, windows, ranks, taps and constants that nobody chose by hand: whole prompts (one of
+    300 tokens, which the walks cut into parts), mixed batches and decoded tails, in both precisions."""
+    drawn = cases.random_config(seed)
+    for dtype, tol in (("float32", 2e-4), ("bfloat16", 6e-2)):
+        folder = cases.write_folder(str(tmp_path / dtype), drawn, seed=seed, dtype=torch.float32 if dtype == "float32" else torch.bfloat16)
+        cfg, w = cases.read_folder(folder)
+        requests = {f"r{i}": helpers.random_tokens(cfg["vocab"], n, seed * 10 + i) for i, n in enumerate((33, 1, 300, 9, 70, 2))}
+        ref = {rid: _plain(cfg, w, toks) for rid, toks in requests.items()}
+        for make_steps in (helpers.steps_whole, helpers.steps_mixed, helpers.steps_decode_tail):
+            steps = make_steps(requests)
+            pages = -(-helpers.max_live_tokens(requests, steps, rounding=16) // 16)
+            engine = build_engine(folder, EngineConfig(dtype=dtype, page_size=16, num_pages=pages, max_batch_size=4, max_seq_len=512,
+                                                       device=DEV))
+            for grp in engine.cache.groups:
+                if grp.pool is not None:
+                    for t in grp.storage.values():
+                        t.fill_(float("nan"))
+            got = helpers.run_steps(engine, steps)
+            engine.cache.audit()
+            rows = torch.cat([(got[rid] - ref[rid]).abs().amax(dim=-1) / float(ref[rid].abs().max()) for rid in ref])
+            if dtype == "float32":
+                assert float(rows.max()) < tol, (make_steps.__name__, float(rows.max()))
+            else:
+                assert float((rows < tol).float().mean()) >= 0.9 and float(rows.median()) < tol / 2, make_steps.__name__
+            engine.close()
+
+
 def test_long_decoding_through_captured_steps(tmp_path):
     """300 decoded tokens after a prompt of 40, three requests side by side: states, convolution tails, kept inputs, window
     edges and the pages given back behind them, step after step through replays of captured steps."""
