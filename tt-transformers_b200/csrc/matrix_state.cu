@@ -223,8 +223,8 @@ struct MsArgs {
 
 template <bool DELTA> static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream);
 
-template <int DR, bool DELTA, bool BIG>
-__global__ void __launch_bounds__(BIG ? MS_MAX_THREADS : 512, DR == 8 ? 2 : 1)
+template <int DR, bool DELTA, int CAP>
+__global__ void __launch_bounds__(CAP, DR == 8 ? 2 : 1)
 matrix_state_walk_kernel(const MsArgs p) {
     extern __shared__ __align__(16) float ms_smem[];
     const int D = p.D, V = p.V, R = p.R;
@@ -304,10 +304,30 @@ matrix_state_walk_kernel(const MsArgs p) {
             const float* a = sa + tt * D;
             const float* b = sb + tt * D;
             const float* w = sw + tt * D;
-            float* mine = part_sums + (size_t)turn * R * VA;
+            // the sum of a column over its row groups: through shared memory (buffers in turn, one barrier), or, where a
+            // thread holds the whole column (R == 1), the thread's own number and no barrier at all
+#define MS_COLUMN_SUM(result, mine_value, everybody)                                             \
+            do {                                                                                 \
+                if (R == 1) {                                                                    \
+                    result = (mine_value);                                                       \
+                } else {                                                                         \
+                    float* slot_ = part_sums + (size_t)turn * R * VA;                            \
+                    if (active) slot_[grp * VA + col] = (mine_value);                            \
+                    __syncthreads();                                                             \
+                    float total_ = 0.f;                                                          \
+                    if ((everybody) || grp == 0) {      /* up to eight groups without a loop */  \
+                        _Pragma("unroll")                                                        \
+                        for (int g = 0; g < 8; ++g)                                              \
+                            if (g < R) total_ += slot_[g * VA + col];                            \
+                        for (int g = 8; g < R; ++g) total_ += slot_[g * VA + col];               \
+                    }                                                                            \
+                    result = total_;                                                             \
+                    turn ^= 1;                                                                   \
+                }                                                                                \
+            } while (0)
             if (DELTA) {
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};              // four chains side by side instead of one of DR links
                 if (active) {
-                    float s4[4] = {0.f, 0.f, 0.f, 0.f};          // four chains side by side instead of one of DR links
 #pragma unroll
                     for (int i = 0; i < DR; i += 4) {
                         const float4 wv = ms_row4(w, row0 + i, D, vec), bv = ms_row4(b, row0 + i, D, vec);
@@ -315,14 +335,10 @@ matrix_state_walk_kernel(const MsArgs p) {
                         s4[0] = fmaf(S[i], bv.x, s4[0]); s4[1] = fmaf(S[i + 1], bv.y, s4[1]);
                         s4[2] = fmaf(S[i + 2], bv.z, s4[2]); s4[3] = fmaf(S[i + 3], bv.w, s4[3]);
                     }
-                    mine[grp * VA + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                 }
-                __syncthreads();
-                float got = 0.f;
-                for (int g = 0; g < R; ++g) got += mine[g * VA + col];
+                float got;
+                MS_COLUMN_SUM(got, (s4[0] + s4[1]) + (s4[2] + s4[3]), true);
                 const float d = sbeta[tt] * ((col < V ? sc[tt * V + col] : 0.f) - got);
-                turn ^= 1;
-                mine = part_sums + (size_t)turn * R * VA;
                 if (p.mode == 1) {                  // end states only: nobody reads this token's output
                     if (active) {
 #pragma unroll
@@ -333,8 +349,8 @@ matrix_state_walk_kernel(const MsArgs p) {
                         }
                     }
                 } else {
+                    s4[0] = s4[1] = s4[2] = s4[3] = 0.f;
                     if (active) {
-                        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                         for (int i = 0; i < DR; i += 4) {
                             const float4 bv = ms_row4(b, row0 + i, D, vec), av = ms_row4(a, row0 + i, D, vec);
@@ -343,15 +359,10 @@ matrix_state_walk_kernel(const MsArgs p) {
                             s4[0] = fmaf(S[i], av.x, s4[0]); s4[1] = fmaf(S[i + 1], av.y, s4[1]);
                             s4[2] = fmaf(S[i + 2], av.z, s4[2]); s4[3] = fmaf(S[i + 3], av.w, s4[3]);
                         }
-                        mine[grp * VA + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                     }
-                    __syncthreads();
-                    if (grp == 0) {
-                        float o = 0.f;
-                        for (int g = 0; g < R; ++g) o += mine[g * VA + col];
-                        so[tt * V + col] = o;
-                    }
-                    turn ^= 1;
+                    float o;
+                    MS_COLUMN_SUM(o, (s4[0] + s4[1]) + (s4[2] + s4[3]), false);
+                    if (grp == 0) so[tt * V + col] = o;
                 }
             } else {
                 const float vc = sc[tt * V + col];
@@ -366,8 +377,8 @@ matrix_state_walk_kernel(const MsArgs p) {
                     }
                     continue;
                 }
+                float s4[4] = {0.f, 0.f, 0.f, 0.f};
                 if (active) {
-                    float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int i = 0; i < DR; i += 4) {
                         const float4 wv = ms_row4(w, row0 + i, D, vec), bv = ms_row4(b, row0 + i, D, vec);
@@ -378,16 +389,12 @@ matrix_state_walk_kernel(const MsArgs p) {
                         S[i] = fmaf(wv.x, S[i], k0); S[i + 1] = fmaf(wv.y, S[i + 1], k1);
                         S[i + 2] = fmaf(wv.z, S[i + 2], k2); S[i + 3] = fmaf(wv.w, S[i + 3], k3);
                     }
-                    mine[grp * V + col] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
                 }
-                __syncthreads();
-                if (grp == 0) {
-                    float o = 0.f;
-                    for (int g = 0; g < R; ++g) o += mine[g * V + col];
-                    so[tt * V + col] = o;
-                }
-                turn ^= 1;
+                float o;
+                MS_COLUMN_SUM(o, (s4[0] + s4[1]) + (s4[2] + s4[3]), false);
+                if (grp == 0) so[tt * V + col] = o;
             }
+#undef MS_COLUMN_SUM
         }
         if (p.mode == 1) continue;
         __syncthreads();
@@ -605,6 +612,8 @@ static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream) {
     const int VA = (DELTA && p.mode == 1) ? V + D : V;
     if (VA > MS_MAX_THREADS) return TTB_ERR_UNSUPPORTED;
     // the fewest rows a thread that still lets a column's row groups fit one block, and at most 512 threads where that works
+    // (a thread that holds a whole column needs no barrier, but its sums are chains as long as the column: measured at
+    // 64 x 64 and 128 x 128, 871 against 635 us and 2,105 against 2,011 us a call of 2,048 tokens)
     int DR = 8;
     while (DR < 64 && VA * ((D + DR - 1) / DR) > 512) DR *= 2;
     const int R = (D + DR - 1) / DR;
@@ -615,18 +624,18 @@ static int ms_launch_mode(MsArgs& p, int segments, cudaStream_t stream) {
     const size_t smem = ((size_t)MS_TILE * (3 * D + 2 * V) + 2 * (size_t)R * (V + (DELTA ? D : 0)) + MS_TILE + D + 2 * MS_TILE) * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
     dim3 grid(segments, p.heads, p.mode == 0 ? 1 : p.parts);
-#define MS_GO(DRV, BIGV)                                                                                             \
+#define MS_GO(DRV, CAPV)                                                                                             \
     do {                                                                                                             \
         static TtbOncePerDevice once;                                                                                \
         if (smem > 48 * 1024 && once.pending()) {                                                                    \
-            cudaFuncSetAttribute(matrix_state_walk_kernel<DRV, DELTA, BIGV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
+            cudaFuncSetAttribute(matrix_state_walk_kernel<DRV, DELTA, CAPV>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
             once.mark();                                                                                             \
         }                                                                                                            \
-        ttb_launch(matrix_state_walk_kernel<DRV, DELTA, BIGV>, grid, threads, smem, stream, p);                      \
+        ttb_launch(matrix_state_walk_kernel<DRV, DELTA, CAPV>, grid, threads, smem, stream, p);                      \
     } while (0)
-    // more than 512 threads only where sixty-four rows a thread still leave that many columns and row groups
-    if (DR == 8) MS_GO(8, false); else if (DR == 16) MS_GO(16, false); else if (DR == 32) MS_GO(32, false);
-    else if (threads <= 512) MS_GO(64, false); else MS_GO(64, true);
+    // sixty-four rows a thread want registers: the fewer threads a block has, the more of them a thread may use
+    if (DR == 8) MS_GO(8, 512); else if (DR == 16) MS_GO(16, 512); else if (DR == 32) MS_GO(32, 512);
+    else if (threads <= 256) MS_GO(64, 256); else if (threads <= 512) MS_GO(64, 512); else MS_GO(64, 1024);
 #undef MS_GO
     return ttb_launch_status();
 }
