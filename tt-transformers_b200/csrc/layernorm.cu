@@ -212,6 +212,75 @@ add_layernorm_sum_kernel(float* __restrict__ residual, const LnTerms terms, cons
         o[c] = from_float<TO>((row[c] - mean) * rstd * norm_w[c] + (norm_b != nullptr ? norm_b[c] : 0.f));
 }
 
+// Rows of up to LN_THREADS * 8 elements (a multiple of 8), everything 16-byte aligned: a thread keeps its eight values in
+// registers through the sum and the norm, and every load is issued before the first is used.
+template <typename TO>
+__global__ void __launch_bounds__(LN_THREADS)
+add_layernorm_sum_regs_kernel(float* __restrict__ residual, const LnTerms terms, const float* __restrict__ row_vector, float row_scale,
+                              const float* __restrict__ norm_w, const float* __restrict__ norm_b, float norm_eps,
+                              TO* __restrict__ out, int width) {
+    __shared__ float scratch[32];
+    const int c = threadIdx.x * 8;
+    const bool mine = c < width;
+    float nw[8], nb[8], rv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { nw[e] = 1.f; nb[e] = 0.f; rv[e] = 0.f; }
+    if (mine) {                                   // weights, which no kernel writes, before the wait for the kernel in front
+        if (norm_w != nullptr) {
+            load8(norm_w + c, nw);
+            if (norm_b != nullptr) load8(norm_b + c, nb);
+        }
+        if (row_vector != nullptr) load8(row_vector + c, rv);
+    }
+    pdl_wait();
+    pdl_launch_dependents();
+    const size_t at = (size_t)blockIdx.x * width + c;
+    float r[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float d[LN_MAX_TERMS][8];
+    if (mine) {
+        load8(residual + at, r);
+#pragma unroll
+        for (int i = 0; i < LN_MAX_TERMS; ++i) {
+            if (i < terms.count) {
+                if (terms.dtype[i] == TTB_DTYPE_BF16) load8(reinterpret_cast<const __nv_bfloat16*>(terms.ptr[i]) + at, d[i]);
+                else load8(reinterpret_cast<const float*>(terms.ptr[i]) + at, d[i]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < LN_MAX_TERMS; ++i) {
+            if (i < terms.count) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) r[e] = fmaf(terms.scale[i], d[i][e], r[e]);
+            }
+        }
+        if (row_vector != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) r[e] = fmaf(row_scale, rv[e], r[e]);
+        }
+        if (terms.count > 0 || row_vector != nullptr) store8(residual + at, r);
+    }
+    if (norm_w == nullptr) return;
+    const float inv_width = 1.f / (float)width;
+    float s = 0.f;
+    if (mine) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) s += r[e];
+    }
+    const float mean = block_sum(s, scratch) * inv_width;
+    float q = 0.f;
+    if (mine) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) { r[e] -= mean; q += r[e] * r[e]; }
+    }
+    const float rstd = rsqrtf(block_sum(q, scratch) * inv_width + norm_eps);
+    if (mine) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = r[e] * rstd * nw[e] + nb[e];
+        store8(out + at, o);
+    }
+}
+
 TTB_EXPORT int ttb_add_layernorm_sum(float* residual, const void* const* term_ptrs, const int* term_dtypes, const float* term_scales,
                                      int count, const float* row_vector, float row_scale, const float* norm_w, const float* norm_b,
                                      float norm_eps, void* out, int out_dtype, int rows, int width, cudaStream_t stream) {
@@ -225,6 +294,18 @@ TTB_EXPORT int ttb_add_layernorm_sum(float* residual, const void* const* term_pt
     }
     const size_t smem = (size_t)width * sizeof(float);
     if (smem > 200 * 1024) return TTB_ERR_UNSUPPORTED;
+    bool regs = (width & 7) == 0 && width <= LN_THREADS * 8 && aligned16(residual) && (!row_vector || aligned16(row_vector)) &&
+                (!norm_w || aligned16(norm_w)) && (!norm_b || aligned16(norm_b)) && (!out || aligned16(out));
+    for (int i = 0; i < count; ++i) regs = regs && aligned16(term_ptrs[i]);
+    if (regs && (out_dtype == TTB_DTYPE_BF16 || out_dtype == TTB_DTYPE_F32 || !norm_w)) {
+        if (out_dtype == TTB_DTYPE_F32 && norm_w)
+            ttb_launch(add_layernorm_sum_regs_kernel<float>, rows, LN_THREADS, 0, stream, residual, terms, row_vector, row_scale, norm_w,
+                       norm_b, norm_eps, (float*)out, width);
+        else
+            ttb_launch(add_layernorm_sum_regs_kernel<__nv_bfloat16>, rows, LN_THREADS, 0, stream, residual, terms, row_vector, row_scale,
+                       norm_w, norm_b, norm_eps, (__nv_bfloat16*)out, width);
+        return ttb_launch_status();
+    }
     if (out_dtype == TTB_DTYPE_BF16 || !norm_w) {
         if (smem > 48 * 1024) cudaFuncSetAttribute(add_layernorm_sum_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         ttb_launch(add_layernorm_sum_kernel<__nv_bfloat16>, rows, LN_THREADS, smem, stream, residual, terms, row_vector, row_scale,

@@ -53,11 +53,12 @@ token_shift_kernel(const void* __restrict__ x, int dtype, int ldx, const float* 
                    const void* __restrict__ kept, void* __restrict__ out, int tokens, int width) {
     pdl_wait();
     pdl_launch_dependents();
+    // blockIdx.y: which run of 256 columns (a handful of tokens still fill the device with blocks)
     for (int t = blockIdx.x; t < tokens; t += gridDim.x) {
         const int seg = seg_of_token[t];
         const bool first = t == cu_seqlens[seg];
         const size_t kept_row = (size_t)slots[seg] * width;
-        for (int c = threadIdx.x; c < width; c += blockDim.x) {
+        for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < width; c += gridDim.y * blockDim.x) {
             const float cur = ms_load(x, dtype, (size_t)t * ldx + c);
             const float before = first ? ms_load(kept, dtype, kept_row + c) : ms_load(x, dtype, (size_t)(t - 1) * ldx + c);
             const float diff = before - cur;
@@ -73,8 +74,9 @@ TTB_EXPORT int ttb_token_shift(const void* x, int dtype, int ldx, const float* m
     if (tokens == 0) return TTB_OK;
     if (!x || !mu || !seg_of_token || !cu_seqlens || !slots || !kept || !out || mixes < 1 || width < 1) return TTB_ERR_ARGUMENT;
     if (dtype != TTB_DTYPE_BF16 && dtype != TTB_DTYPE_F32) return TTB_ERR_UNSUPPORTED;
-    ttb_launch(token_shift_kernel, tokens < 148 * 8 ? tokens : 148 * 8, 256, 0, stream, x, dtype, ldx, mu, mixes, seg_of_token,
-               cu_seqlens, slots, kept, out, tokens, width);
+    const int runs = tokens >= 148 * 4 ? 1 : (width + 255) / 256 < 64 ? (width + 255) / 256 : 64;
+    ttb_launch(token_shift_kernel, dim3(tokens < 148 * 8 ? tokens : 148 * 8, runs), 256, 0, stream, x, dtype, ldx, mu, mixes,
+               seg_of_token, cu_seqlens, slots, kept, out, tokens, width);
     return ttb_launch_status();
 }
 
